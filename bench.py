@@ -1,0 +1,505 @@
+#!/usr/bin/env python
+"""Benchmark of the MoE feed-forward block on B200 (driver contract).
+
+Headline workload: a stack of 30 independently seeded
+Gemma-4-26B-A4B-like MoE layers (D=2816, F=704, E=128, top-8, GeGLU, int4
+symmetric group-32 experts with fp16 scales, fp32 router on the RMSNorm'd
+input), decoded at T=1.  One step = the 30-layer stack over one token batch:
+layer l+1 reads layer l's bf16 output.  The step is captured once in a CUDA
+graph and replayed.  Metric: MoE-layer tokens per second (tokens x layers /
+s).  The weights one step touches (30 x 8 experts x 3.35 MB = 803 MB) are
+larger than the 126 MB L2, so no L2 flush is needed between steps.
+
+Also reported on the same GPU: decode at T=4/16/64 and prefill at T=4096
+with Zipf(1.1) routing skew, each as layer-tokens/s.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With --gpus N > 1 (launched by torch.distributed.run) every rank runs the
+same decode stack on its own GPU with its own tokens (data-parallel replicas,
+weak scaling: decode needs no exchange between GPUs); the timed region is
+bracketed by barriers and the max over ranks is used.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG = "gemma"
+D, F, E, K = 2816, 704, 128, 8
+LAYERS = 30
+EXPERT_BYTES = 3 * (F * D // 2 + F * (D // 32) * 2)  # 3,345,408
+GATE_UP_BYTES_PER_EXPERT = 2 * (F * D // 2 + F * (D // 32) * 2)
+DOWN_BYTES_PER_EXPERT = D * F // 2 + D * (F // 32) * 2
+ROUTER_BYTES = E * D * 4
+METRIC = "MoE-layer tokens/s (Gemma-4-26B-A4B-like layer, decode T=1, 30-layer stack)"
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return self
+
+        def reader():
+            for line in self.proc.stdout:
+                self.rows.append([c.strip() for c in line.split(",")])
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        return self
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() in ("active", "1"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": float(max(mx)) if mx else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+def build_stack(ctx, n_layers: int, skew, device, seed0: int):
+    import tsugumi_b200 as tb
+    from tsugumi_b200.synthetic import device_layer_tensors
+
+    layers = []
+    for l in range(n_layers):
+        t = device_layer_tensors(CFG, seed0 + 7919 * l, skew, device)
+        layers.append(tb.MoELayer(ctx, t))
+    return layers
+
+
+def distinct_experts(ctx, layers, x0, T):
+    """Runs the stack once un-captured and counts the distinct experts each
+    layer reads (u(T), the unit of the decode roofline)."""
+    import torch
+    import tsugumi_b200 as tb
+
+    us = []
+    x = x0
+    for lay in layers:
+        ids = torch.empty((T, K), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, K), dtype=torch.float32, device=x.device)
+        tb.MoE(ctx, lay).encode_router_gemma4_bf16(x, ids, w)
+        y = lay.forward(x)
+        ctx.sync()
+        us.append(int(torch.unique(ids).numel()))
+        x = y
+    return us
+
+
+def capture_stack(ctx, layers, x_in, profile: bool):
+    import torch
+
+    T = x_in.shape[0]
+    bufs = [torch.empty((T, D), dtype=torch.bfloat16, device=x_in.device) for _ in range(2)]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        ctx.set_stream(side)
+        if profile:
+            from tsugumi_b200 import _abi
+            _abi.check(ctx.lib.tsg_ctx_profile_begin(ctx.h, len(layers)), ctx.h)
+        with torch.cuda.graph(g, stream=side):
+            x = x_in
+            for i, lay in enumerate(layers):
+                y = bufs[i % 2]
+                lay.forward(x, y=y)
+                x = y
+    torch.cuda.current_stream().wait_stream(side)
+    ctx.set_stream(torch.cuda.current_stream())
+    return g, x
+
+
+def profile_read(ctx):
+    import ctypes as C
+    from tsugumi_b200 import _abi
+
+    ms = (C.c_float * 4)()
+    n = C.c_uint32()
+    _abi.check(ctx.lib.tsg_ctx_profile_end(ctx.h, ms, C.byref(n)), ctx.h)
+    return list(ms), n.value
+
+
+def timed_replays(g, steps, warmup, barrier=None):
+    import torch
+
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    return start.elapsed_time(end) / steps
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import tsugumi_b200 as tb
+    from tsugumi_b200.synthetic import bf16_bits_to_f32  # noqa: F401
+
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://",
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    barrier = (lambda: dist.barrier(device_ids=[local])) if world > 1 else None
+
+    ctx = tb.Context(local)
+    ctx.set_stream(torch.cuda.current_stream())
+    layers = build_stack(ctx, LAYERS, None, device, seed0=1)
+    T = 1
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    x0 = torch.randn((T, D), generator=gen, device=device).to(torch.bfloat16)
+    ctx.reserve(layers[0], 4096)
+    torch.cuda.synchronize()
+
+    us = distinct_experts(ctx, layers, x0, T)
+    g, y_last = capture_stack(ctx, layers, x0, profile=True)
+    clocks = ClockSampler(local).start()
+    ms = timed_replays(g, args.steps, args.warmup, barrier)
+    clk = clocks.stop()
+    stage_ms, ncalls = profile_read(ctx)
+    ms_t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * T * LAYERS / (ms_max / 1e3)
+
+    # dominant kernel: the decode gate/up kernel (stage 1), averaged over the
+    # 30 launches of the last timed replay
+    pk = peaks()
+    u_mean = float(np.mean(us))
+    gu_ms = stage_ms[1] / max(ncalls, 1)
+    down_ms = stage_ms[2] / max(ncalls, 1)
+    gu_bytes = u_mean * GATE_UP_BYTES_PER_EXPERT
+    dn_bytes = u_mean * DOWN_BYTES_PER_EXPERT
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    layer_ms = sum(stage_ms) / max(ncalls, 1)
+    layer_gbs = u_mean * EXPERT_BYTES / (layer_ms / 1e3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "ncu_traffic.json"
+    if tfile.exists():
+        tj = json.loads(tfile.read_text())
+        traffic = tj.get("decode_gate_up_t1_bytes_per_launch")
+
+    # end to end through the public API: pinned host input -> stack -> host
+    x_host = torch.empty((T, D), dtype=torch.bfloat16, pin_memory=True)
+    x_host.copy_(x0.cpu())
+    y_host = torch.empty((T, D), dtype=torch.bfloat16, pin_memory=True)
+    for _ in range(args.warmup):
+        x0.copy_(x_host, non_blocking=True)
+        g.replay()
+        y_host.copy_(y_last, non_blocking=True)
+        torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        x0.copy_(x_host, non_blocking=True)
+        g.replay()
+        y_host.copy_(y_last, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    e2e_t = torch.tensor([e2e_ms], device=device)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = world * T * LAYERS / (float(e2e_t.item()) / 1e3)
+    del g
+
+    sweep = {}
+    if not args.no_sweep:
+        sweep = run_sweep(ctx, layers, device, args, barrier)
+
+    result = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "layer-tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4w-f32acc",
+        "data": "synthetic (seeded; BASELINE value distributions)",
+        "config": {
+            "workload": "gemma-like MoE layer decode, T=1, 30-layer stack (configs[1])",
+            "D": D, "F": F, "E": E, "top_k": K, "layers": LAYERS, "tokens_per_step": T,
+            "act": "GeGLU (gelu tanh)", "weights": "int4 sym group-32, fp16 scales",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "no flush: each step reads 803 MB of expert weights (> 126 MB L2)",
+            "graph": "CUDA graph of the 30-layer step",
+        },
+        "roofline": {
+            "kernel": "decode_gate_up_kernel (T=1)",
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": pk["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"],
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": gu_bytes,
+            "avg_launch_ms": gu_ms,
+            "peak_source": pk["source"],
+            "layer": {"ms": layer_ms, "expert_bytes": u_mean * EXPERT_BYTES,
+                      "gbs": layer_gbs, "frac": layer_gbs / pk["hbm_gbs"],
+                      "stage_ms": {"router": stage_ms[0] / max(ncalls, 1), "gate_up": gu_ms,
+                                   "down_combine": down_ms}},
+        },
+        "e2e": {"value": e2e_value, "unit": "layer-tokens/s",
+                "h2d_bytes_per_step": T * D * 2, "d2h_bytes_per_step": T * D * 2},
+        "gpu_launches": 3 * LAYERS * args.steps,
+        "clocks": clk,
+        "sweep": sweep,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        result["cpu_baseline"] = cpu_baseline_sample(layers[:2], seconds=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_sweep(ctx, layers, device, args, barrier):
+    """Other decode batch sizes and the prefill regime on the same stack."""
+    import torch
+
+    out = {}
+    pk = peaks()
+    steps = max(3, args.steps // 4)
+    for T in (4, 16, 64):
+        gen = torch.Generator(device=device)
+        gen.manual_seed(2000 + T)
+        x0 = torch.randn((T, D), generator=gen, device=device).to(torch.bfloat16)
+        us = distinct_experts(ctx, layers, x0, T)
+        g, _ = capture_stack(ctx, layers, x0, profile=False)
+        ms = timed_replays(g, steps, 3, barrier)
+        del g
+        bytes_ = float(np.mean(us)) * EXPERT_BYTES * LAYERS
+        gbs = bytes_ / (ms / 1e3) / 1e9
+        out[f"decode_T{T}"] = {"layer_tokens_per_s": T * LAYERS / (ms / 1e3), "ms_per_step": ms,
+                               "u_mean": float(np.mean(us)), "expert_gbs": gbs,
+                               "hbm_frac": gbs / pk["hbm_gbs"]}
+    # prefill, Zipf(1.1) skew, fewer layers (per-layer cost is identical)
+    import tsugumi_b200 as tb
+    from tsugumi_b200.synthetic import device_layer_tensors
+
+    n_pre = 4
+    pre_layers = [tb.MoELayer(ctx, device_layer_tensors(CFG, 91 + l, 1.1, device))
+                  for l in range(n_pre)]
+    T = 4096
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4096)
+    x0 = torch.randn((T, D), generator=gen, device=device).to(torch.bfloat16)
+    ctx.reserve(pre_layers[0], T)
+    y = torch.empty((T, D), dtype=torch.bfloat16, device=device)
+    for lay in pre_layers:  # warm (workspace, module load)
+        lay.forward(x0, y=y)
+    torch.cuda.synchronize()
+    from tsugumi_b200 import _abi
+    _abi.check(ctx.lib.tsg_ctx_profile_begin(ctx.h, n_pre * steps), ctx.h)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        for lay in pre_layers:
+            lay.forward(x0, y=y)
+    e1.record()
+    torch.cuda.synchronize()
+    stage_ms, ncalls = profile_read(ctx)
+    ms_layer = e0.elapsed_time(e1) / (steps * n_pre)
+    flops = 2.0 * T * K * 3 * D * F
+    gu = stage_ms[1] / max(ncalls, 1)
+    dn = stage_ms[2] / max(ncalls, 1)
+    out["prefill_T4096_zipf1.1"] = {
+        "layer_tokens_per_s": T / (ms_layer / 1e3), "ms_per_layer": ms_layer,
+        "routed_tflops": flops / (ms_layer / 1e3) / 1e12,
+        "tensor_frac": flops / (ms_layer / 1e3) / 1e12 / pk["bf16_tflops"],
+        "stage_ms": {"router_permute_gather": stage_ms[0] / max(ncalls, 1), "gate_up": gu,
+                     "down": dn, "combine": stage_ms[3] / max(ncalls, 1)},
+        "gate_up_tflops": (2.0 * T * K * 2 * D * F) / (gu / 1e3) / 1e12,
+        "down_tflops": (2.0 * T * K * D * F) / (dn / 1e3) / 1e12,
+    }
+    return out
+
+
+def cpu_baseline_sample(layers, seconds: float = 12.0) -> dict:
+    """The CPU oracle (restated reference CPU path) on a bounded sample of the
+    same workload: T=1 tokens through copies of two of the stack's layers."""
+    from oracle import oracle as O
+    from tsugumi_b200.synthetic import f32_to_bf16_bits, to_host_layer
+
+    hosts = [O.OracleLayer(to_host_layer(l.t)) for l in layers]
+    rng = np.random.default_rng(0)
+    x = f32_to_bf16_bits(rng.standard_normal((1, D)).astype(np.float32))
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for h in hosts:
+            y, _, _ = h.block(x)
+            x = f32_to_bf16_bits(y)
+            n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "layer-tokens/s", "cores": O.num_threads(),
+            "kind": "port",
+            "sample": f"{n} layer-tokens (T=1, 2 of the 30 layers, alternating) in {dt:.1f} s"}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU path (restated: the reference is Swift +
+# Metal, which has no toolchain here) on the host cores
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    from tsugumi_b200.synthetic import f32_to_bf16_bits, host_layer
+
+    n_layers = 4
+    hosts = [O.OracleLayer(host_layer(CFG, 1 + 7919 * l)) for l in range(n_layers)]
+    rng = np.random.default_rng(1000)
+    x = f32_to_bf16_bits(rng.standard_normal((1, D)).astype(np.float32))
+
+    def step(x):
+        for h in hosts:
+            y, _, _ = h.block(x)
+            x = f32_to_bf16_bits(y)
+        return x
+
+    for _ in range(args.warmup):
+        x = step(x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        x = step(x)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = n_layers / dt
+    result = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "layer-tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f64acc",
+        "data": "synthetic (seeded; BASELINE value distributions)",
+        "config": {"workload": "gemma-like MoE layer decode, T=1 (configs[1])", "D": D, "F": F,
+                   "E": E, "top_k": K, "sample_layers": n_layers},
+        "cpu_baseline": {"value": value, "unit": "layer-tokens/s", "cores": O.num_threads(),
+                         "kind": "port",
+                         "sample": f"T=1 through {n_layers} layers per step (stack of 30 has "
+                                   "identical per-layer cost)"},
+        "e2e": {"value": value, "unit": "layer-tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,289 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bars:
+  * expert ids and permutation / index arrays bit-exact, except tokens whose
+    K-th / (K+1)-th logit gap is below 1e-6;
+  * block outputs within relative L2 error 2e-3 of the fp32-accumulated
+    oracle.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import tsugumi_b200 as tb  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+from tsugumi_b200.synthetic import host_layer, host_tokens  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 2e-3
+TIE_GAP = 1e-6
+
+
+def rel_l2(a, b) -> float:
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = tb.Context(0)
+    yield c
+    c.close()
+
+
+_LAYERS: dict = {}
+
+
+def layer_pair(ctx, name, seed, skew=None):
+    key = (name, seed, skew)
+    if key not in _LAYERS:
+        host = host_layer(name, seed, skew=skew)
+        dev = tb.MoELayer(ctx, tb.upload_host_layer(host))
+        _LAYERS[key] = (host, dev, O.OracleLayer(host))
+    return _LAYERS[key]
+
+
+def gpu_route(ctx, layer, x_dev):
+    T = x_dev.shape[0]
+    ids = torch.empty((T, layer.top_k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, layer.top_k), dtype=torch.float32, device="cuda")
+    w16 = torch.empty((T, layer.top_k), dtype=torch.float16, device="cuda")
+    tb.MoE(ctx, layer).encode_router_gemma4_bf16(x_dev, ids, w, w16)
+    ctx.sync()
+    return ids, w, w16
+
+
+def to_dev(x_np):
+    return torch.from_numpy(x_np.view(np.int16)).to("cuda").view(torch.bfloat16)
+
+
+ROUTER_CASES = [
+    ("tiny", 16, None, 64),
+    ("gemma", 1, None, 64),
+    ("gemma", 4, None, 64),
+    ("gemma", 64, None, 64),
+    ("gemma", 256, 1.1, 64),
+    ("qwen", 16, None, 64),
+    ("qwen", 300, None, 64),
+    ("tiny", 40, None, 0),  # prefill router kernels on a small batch
+]
+
+
+@pytest.mark.parametrize("name,T,skew,dmax", ROUTER_CASES)
+def test_router_topk_matches_oracle(ctx, name, T, skew, dmax):
+    host, dev, ol = layer_pair(ctx, name, 11, skew)
+    ctx.set_decode_max_tokens(dmax)
+    try:
+        x = host_tokens(T, host.d, 100 + T)
+        ids, w, w16 = gpu_route(ctx, dev, to_dev(x))
+    finally:
+        ctx.set_decode_max_tokens(64)
+    ref_ids, ref_w, gap, _ = ol.router(x)
+    ok = gap >= TIE_GAP
+    assert ok.sum() >= T - 1
+    g_ids = ids.cpu().numpy().astype(np.uint32)
+    assert np.array_equal(g_ids[ok], ref_ids[ok])
+    assert np.max(np.abs(w.cpu().numpy()[ok] - ref_w[ok])) < 2e-6
+    assert np.max(np.abs(w16.float().cpu().numpy()[ok] - ref_w[ok])) < 1e-3
+
+
+def _np_pairs(rows):
+    a = np.zeros((len(rows), 4), np.int32)
+    for i, r in enumerate(rows):
+        a[i] = r
+    return a
+
+
+def test_grouping_golden_case_on_gpu(ctx):
+    rows = [(0, 3, 0, 10), (0, 1, 1, 11), (0, 4, 2, 12), (1, 1, 0, 13), (1, 3, 1, 14),
+            (1, 2, 2, 15), (2, 4, 0, 16), (2, 3, 1, 17), (2, 1, 2, 18), (3, 5, 0, 19),
+            (3, 1, 1, 20), (3, 4, 2, 21)][::-1]
+    pairs = torch.from_numpy(_np_pairs(rows)).cuda()
+    g = tb.PrefillMoEGrouping.group_token_expert_pairs(ctx, pairs, 4, 3, 6, tile_expert_count=2)
+    assert list(g.sorted_pairs[:, 1]) == [1, 1, 1, 1, 2, 3, 3, 3, 4, 4, 4, 5]
+    assert g.sorted_pairs[:, [0, 2]].tolist() == [
+        [0, 1], [1, 0], [2, 2], [3, 1], [1, 2], [0, 0], [1, 1], [2, 1], [0, 2], [2, 0], [3, 2],
+        [3, 0]]
+    assert list(g.per_expert_offsets) == [0xFFFFFFFF, 0, 4, 5, 8, 11]
+    assert list(g.per_expert_counts) == [0, 4, 1, 3, 3, 1]
+    assert g.groups.tolist() == [[1, 0, 4], [2, 4, 1], [3, 5, 3], [4, 8, 3], [5, 11, 1]]
+    assert g.tiles.tolist() == [[0, 2, 0, 5], [2, 2, 5, 6], [4, 1, 11, 1]]
+    assert g.max_pairs_per_expert == 4 and g.max_pairs_per_tile == 6
+    assert g.max_live_experts_per_tile == 2
+
+
+@pytest.mark.parametrize("T,K,E,tec,keys,brk", [
+    (37, 4, 16, 16, False, None),
+    (512, 8, 128, 16, False, None),
+    (300, 8, 256, 5, True, None),
+    (64, 6, 40, 4, False, 3),
+    (4096, 8, 128, 16, False, None),
+])
+def test_grouping_matches_oracle(ctx, T, K, E, tec, keys, brk):
+    rng = np.random.default_rng(T + K)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.uint32)
+    w16 = rng.integers(0, 0x3C00, (T, K)).astype(np.uint16)
+    pairs = O.make_pairs(ids, w16)
+    perm = rng.permutation(T * K)
+    shuffled = pairs[perm]
+    sort_keys = rng.integers(0, 5, E).astype(np.uint64) if keys else None
+    ref = O.group_pairs(shuffled, T, K, E, tec, sort_keys, brk)
+    p = np.stack([shuffled[f].astype(np.int64) for f in ("token", "expert", "rank",
+                                                          "weight_bits")], 1).astype(np.int32)
+    g = tb.PrefillMoEGrouping.group_token_expert_pairs(
+        ctx, torch.from_numpy(p).cuda(), T, K, E, tec,
+        None if sort_keys is None else sort_keys, brk)
+    got = g.sorted_pairs
+    assert np.array_equal(got[:, 0], ref["sorted_pairs"]["token"])
+    assert np.array_equal(got[:, 1], ref["sorted_pairs"]["expert"])
+    assert np.array_equal(got[:, 2], ref["sorted_pairs"]["rank"])
+    assert np.array_equal(got[:, 3], ref["sorted_pairs"]["weight_bits"])
+    assert np.array_equal(g.per_expert_offsets, ref["offsets"])
+    assert np.array_equal(g.per_expert_counts, ref["counts"])
+    assert g.groups.tolist() == [list(x) for x in ref["groups"].tolist()]
+    assert g.tiles.tolist() == [list(x) for x in ref["tiles"].tolist()]
+
+
+@pytest.mark.parametrize("rows,args,msg", [
+    ([(0, 2, 0, 1)], (1, 1, 2), "expert 2 is out of range"),
+    ([(0, 0, 0, 1), (0, 1, 0, 2)], (1, 2, 2), "duplicate route pair for token 0"),
+    ([(3, 0, 0, 1)], (1, 1, 2), "token 3 is out of range"),
+])
+def test_grouping_rejects_invalid_pairs(ctx, rows, args, msg):
+    with pytest.raises(tb.PrefillMoEGroupingError, match=msg):
+        tb.PrefillMoEGrouping.group_token_expert_pairs(
+            ctx, torch.from_numpy(_np_pairs(rows)).cuda(), *args, tile_expert_count=1)
+
+
+def test_grouping_rejects_bad_arguments(ctx):
+    p = torch.from_numpy(_np_pairs([(0, 0, 0, 1)])).cuda()
+    with pytest.raises(tb.PrefillMoEGroupingError, match="tileExpertCount must be in 1...16, got 17"):
+        tb.PrefillMoEGrouping.group_token_expert_pairs(ctx, p, 1, 1, 1, tile_expert_count=17)
+    with pytest.raises(tb.PrefillMoEGroupingError, match="expected 2 expert sort keys, got 1"):
+        tb.PrefillMoEGrouping.group_token_expert_pairs(ctx, p, 1, 1, 2, 1, expert_sort_keys=[0])
+
+
+BLOCK_CASES = [
+    # name, T, skew, decode_max_tokens, oracle token sample
+    ("tiny", 16, None, 64, None),
+    ("gemma", 1, None, 64, None),
+    ("gemma", 4, None, 64, None),
+    ("gemma", 16, None, 64, None),
+    ("gemma", 64, None, 64, None),
+    ("qwen", 1, None, 64, None),
+    ("qwen", 64, None, 64, None),
+    ("tiny", 200, None, 64, None),
+    ("gemma", 512, None, 64, 48),
+    ("gemma", 4096, 1.1, 64, 48),
+    ("qwen", 1024, None, 64, 48),
+    ("gemma", 48, None, 0, None),  # prefill kernels at a decode size
+]
+
+
+@pytest.mark.parametrize("name,T,skew,dmax,sample", BLOCK_CASES)
+def test_block_forward_matches_oracle(ctx, name, T, skew, dmax, sample):
+    host, dev, ol = layer_pair(ctx, name, 11, skew)
+    x = host_tokens(T, host.d, 7 + T)
+    xd = to_dev(x)
+    ctx.set_decode_max_tokens(dmax)
+    try:
+        ids, w, _ = gpu_route(ctx, dev, xd)
+        y = dev.forward(xd, out_dtype=torch.float32)
+        ctx.sync()
+    finally:
+        ctx.set_decode_max_tokens(64)
+    rows = np.arange(T) if sample is None else np.linspace(0, T - 1, sample).astype(int)
+    y_ref, _, _ = ol.block(x[rows], ids.cpu().numpy()[rows].astype(np.uint32),
+                           w.cpu().numpy()[rows])
+    y_gpu = y.cpu().numpy()[rows]
+    err = rel_l2(y_gpu, y_ref)
+    print(f"{name} T={T}: rel L2 {err:.3e}")
+    assert np.all(np.isfinite(y_gpu))
+    assert err <= REL_L2
+
+
+@pytest.mark.parametrize("name,T", [("gemma", 8), ("qwen", 32)])
+def test_decode_and_prefill_regimes_agree(ctx, name, T):
+    host, dev, ol = layer_pair(ctx, name, 11, None)
+    xd = to_dev(host_tokens(T, host.d, 3))
+    y_dec = dev.forward(xd, out_dtype=torch.float32)
+    ctx.set_decode_max_tokens(0)
+    try:
+        y_pre = dev.forward(xd, out_dtype=torch.float32)
+        ctx.sync()
+    finally:
+        ctx.set_decode_max_tokens(64)
+    assert rel_l2(y_pre.cpu().numpy(), y_dec.cpu().numpy()) < REL_L2
+
+
+@pytest.mark.parametrize("regime", ["decode", "prefill"])
+def test_experts_with_caller_routing(ctx, regime):
+    host, dev, ol = layer_pair(ctx, "gemma", 11, None)
+    T = 8 if regime == "decode" else 200
+    x = host_tokens(T, host.d, 55)
+    rng = np.random.default_rng(5)
+    ids = np.stack([rng.choice(host.num_experts, host.top_k, replace=False) for _ in range(T)])
+    w = rng.uniform(0.05, 0.3, (T, host.top_k)).astype(np.float32)
+    resid = rng.standard_normal((T, host.d)).astype(np.float32)
+    y = torch.empty((T, host.d), dtype=torch.float32, device="cuda")
+    idt = torch.from_numpy(ids.astype(np.int32)).cuda()
+    wt = torch.from_numpy(w).cuda()
+    rt = torch.from_numpy(resid).cuda()
+    if regime == "decode":
+        tb.MoE(ctx, dev).encode_routed_phases(to_dev(x), idt, wt, y, residual=rt)
+    else:
+        tb.PrefillGroupedRoutedMoE(ctx, dev).encode_streamed_tiled(to_dev(x), idt, wt, y,
+                                                                   residual=rt)
+    ctx.sync()
+    y_ref, _, _ = ol.block(x, ids.astype(np.uint32), w)
+    assert rel_l2(y.cpu().numpy(), y_ref + resid) <= REL_L2
+
+
+@pytest.mark.parametrize("T", [1, 100])
+def test_shared_expert_alone(ctx, T):
+    host, dev, ol = layer_pair(ctx, "qwen", 11, None)
+    x = host_tokens(T, host.d, 21)
+    y = torch.empty((T, host.d), dtype=torch.float32, device="cuda")
+    tb.SharedExpertRuntime(ctx, dev).encode(to_dev(x), y)
+    ctx.sync()
+    assert rel_l2(y.cpu().numpy(), ol.shared_expert(x)) <= REL_L2
+
+
+def test_reduce_token_major(ctx):
+    rng = np.random.default_rng(2)
+    T, K, D = 33, 8, 512
+    part = rng.standard_normal((T * K, D)).astype(np.float16)
+    w = rng.uniform(0, 1, (T, K)).astype(np.float32)
+    h2 = torch.empty((T, D), dtype=torch.float32, device="cuda")
+    tb.PrefillMoE.encode_reduce_token_major(ctx, torch.from_numpy(part).cuda(),
+                                            torch.from_numpy(w).cuda(), h2)
+    ctx.sync()
+    ref = O.reduce_token_major(part.astype(np.float32), w)
+    assert np.max(np.abs(h2.cpu().numpy() - ref)) < 1e-5
+
+
+def test_make_token_expert_pairs(ctx):
+    ids = torch.tensor([[3, 1], [0, 2]], dtype=torch.int32, device="cuda")
+    w16 = torch.tensor([[1, 2], [3, 4]], dtype=torch.int16, device="cuda")
+    p = tb.PrefillRouter.make_token_expert_pairs(ctx, ids, w16, 2, 2)
+    ctx.sync()
+    assert p.cpu().tolist() == [[0, 3, 0, 1], [0, 1, 1, 2], [1, 0, 0, 3], [1, 2, 1, 4]]
+
+
+def test_bf16_output_and_residual(ctx):
+    host, dev, ol = layer_pair(ctx, "tiny", 11, None)
+    T = 16
+    x = host_tokens(T, host.d, 4)
+    resid = np.random.default_rng(0).standard_normal((T, host.d)).astype(np.float32)
+    xd = to_dev(x)
+    ids, w, _ = gpu_route(ctx, dev, xd)
+    y = dev.forward(xd, residual=torch.from_numpy(resid).cuda(), out_dtype=torch.bfloat16)
+    ctx.sync()
+    y_ref, _, _ = ol.block(x, ids.cpu().numpy().astype(np.uint32), w.cpu().numpy())
+    assert rel_l2(y.float().cpu().numpy(), y_ref + resid) <= REL_L2

@@ -1,0 +1,360 @@
+// permute.cu -- the token->expert permutation on the GPU.
+//
+// Restates PrefillMoEGrouping.groupTokenExpertPairs
+// (Sources/Tsugumi/Kernels/Prefill/MoE/PrefillMoEGrouping.swift:91-201), which
+// the reference runs on the CPU, as three kernels:
+//   1. (caller-supplied pairs only) validate each pair and place it at its
+//      token-major slot token*K + rank; a second pair for the same slot is a
+//      duplicate (PrefillMoEGroupingError.duplicateTokenRank);
+//   2. one CTA per expert counts its pairs; the last CTA to finish orders the
+//      experts (by optional sort key, then index), scans the counts into
+//      offsets (UINT32_MAX for empty experts), and writes the groups, the
+//      tiles of <= tileExpertCount groups (with the optional forced cut) and
+//      the row-tile schedule of the grouped contraction;
+//   3. one CTA per expert walks the token-major pairs in order and writes its
+//      pairs to consecutive sorted positions with block-wide ballots, so the
+//      order inside an expert is (token, rank) -- a stable counting sort.
+// Output is bit-identical to the reference's sort by (key, expert, token,
+// rank).
+#include "tsg_common.cuh"
+#include "tsg_kernels.cuh"
+
+namespace tsg {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Error record: [0] bits, [1] first error code, [2] offending value.
+TSG_DEV void record_error(uint32_t* err, uint32_t code, uint32_t value) {
+  if (!err) return;
+  atomicOr(err, TSG_DEVERR_METADATA);
+  if (atomicCAS(err + 1, 0u, code) == 0u) err[2] = value;
+}
+
+// ---- 1. caller pairs -> token-major slots ----------------------------------
+__global__ void place_pairs_kernel(const Pair* pairs, int n, int T, int K, int E,
+                                   uint32_t* tm_ids, uint16_t* tm_w16, uint32_t* occupied,
+                                   uint32_t* err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const Pair pr = pairs[i];
+  // codes follow PrefillMoEGroupingError: 6 token, 7 rank, 8 expert, 9 duplicate
+  if (pr.token >= static_cast<uint32_t>(T)) { record_error(err, 6u, pr.token); return; }
+  if (pr.rank >= static_cast<uint32_t>(K)) { record_error(err, 7u, pr.rank); return; }
+  if (pr.expert >= static_cast<uint32_t>(E)) { record_error(err, 8u, pr.expert); return; }
+  const uint32_t slot = pr.token * static_cast<uint32_t>(K) + pr.rank;
+  if (atomicExch(&occupied[slot], 1u) != 0u) { record_error(err, 9u, pr.token); return; }
+  tm_ids[slot] = pr.expert;
+  tm_w16[slot] = static_cast<uint16_t>(pr.weight_bits & 0xFFFFu);
+}
+
+// ---- 2. counts + last-CTA scan ---------------------------------------------
+__device__ uint32_t block_sum_u32(uint32_t v, uint32_t* s_tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  if (lane == 0) s_tmp[warp] = v;
+  __syncthreads();
+  uint32_t r = 0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) r += s_tmp[w];
+  __syncthreads();
+  return r;  // valid in thread 0
+}
+
+// Exclusive scan of v over the block (thread order); returns the prefix and
+// writes the block total to *total.
+__device__ uint32_t block_excl_scan(uint32_t v, uint32_t* s_tmp, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  if (lane == 31) s_tmp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < nw ? s_tmp[lane] : 0u;
+    uint32_t wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xFFFFFFFFu, wi, o);
+      if (lane >= o) wi += x;
+    }
+    if (lane < nw) s_tmp[lane] = wi - w;
+    if (lane == nw - 1) s_tmp[32] = wi;
+  }
+  __syncthreads();
+  const uint32_t r = s_tmp[warp] + incl - v;
+  *total = s_tmp[32];
+  __syncthreads();
+  return r;
+}
+
+struct PermuteArgs {
+  const uint32_t* tm_ids;  // [T*K] token-major expert ids
+  int T, K, E, P;
+  int tile_rows, tile_expert_count, tile_break, has_shared;
+  const uint64_t* sort_keys;
+};
+
+__global__ void __launch_bounds__(kThreads) permute_count_kernel(PermuteArgs a, RouteBuffers rb) {
+  __shared__ uint32_t s_tmp[33];
+  __shared__ uint32_t s_last;
+  extern __shared__ uint32_t s_dyn[];  // [3 * E] in the last CTA
+  const int e = blockIdx.x;
+  uint32_t cnt = 0;
+  for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
+    const uint32_t id = a.tm_ids[i];
+    cnt += (id == static_cast<uint32_t>(e)) ? 1u : 0u;
+    if (e == 0 && id >= static_cast<uint32_t>(a.E)) record_error(rb.err, 8u, id);
+  }
+  const uint32_t total = block_sum_u32(cnt, s_tmp);
+  if (threadIdx.x == 0) rb.counts[e] = total;
+
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(rb.sync_counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (threadIdx.x == 0) *rb.sync_counter = 0u;
+
+  const int E = a.E;
+  uint32_t* s_cnt = s_dyn;          // [E]
+  uint32_t* s_order = s_dyn + E;    // [E] order position -> expert
+  uint32_t* s_rank = s_dyn + 2 * E; // [E] expert -> order position
+  for (int x = threadIdx.x; x < E; x += blockDim.x) s_cnt[x] = __ldcg(rb.counts + x);
+  // order experts by (sort key, index): rank = number of experts before it
+  for (int x = threadIdx.x; x < E; x += blockDim.x) {
+    uint32_t r = static_cast<uint32_t>(x);
+    if (a.sort_keys) {
+      const uint64_t kx = a.sort_keys[x];
+      r = 0;
+      for (int y = 0; y < E; ++y) {
+        const uint64_t ky = a.sort_keys[y];
+        r += (ky < kx || (ky == kx && y < x)) ? 1u : 0u;
+      }
+    }
+    s_rank[x] = r;
+    s_order[r] = static_cast<uint32_t>(x);
+  }
+  __syncthreads();
+  // scan counts in order; groups are the non-empty experts in order
+  uint32_t run = 0, grun = 0, trun = 0;
+  const int ntl = a.tile_rows;
+  for (int base = 0; base < E; base += blockDim.x) {
+    const int r = base + threadIdx.x;
+    const uint32_t ex = r < E ? s_order[r] : 0u;
+    const uint32_t c = r < E ? s_cnt[ex] : 0u;
+    uint32_t tot_c, tot_g, tot_t;
+    const uint32_t off = run + block_excl_scan(c, s_tmp, &tot_c);
+    const uint32_t gi = grun + block_excl_scan(c > 0u ? 1u : 0u, s_tmp, &tot_g);
+    const uint32_t nrt = (c + ntl - 1) / ntl;
+    const uint32_t ti = trun + block_excl_scan(nrt, s_tmp, &tot_t);
+    if (r < E) {
+      rb.offsets[ex] = c ? off : 0xFFFFFFFFu;
+      if (c) {
+        rb.groups[gi].expert = ex;
+        rb.groups[gi].pair_start = off;
+        rb.groups[gi].pair_count = c;
+        for (uint32_t j = 0; j < nrt; ++j) {
+          RowTile t;
+          t.expert = ex;
+          t.row_start = off + j * ntl;
+          t.rows = min(static_cast<uint32_t>(ntl), c - j * ntl);
+          t.pad = 0;
+          rb.row_tiles[ti + j] = t;
+        }
+      }
+    }
+    run += tot_c;
+    grun += tot_g;
+    trun += tot_t;
+  }
+  __syncthreads();  // groups written by all threads are read below
+  if (threadIdx.x == 0) {
+    uint32_t nrt = trun;
+    if (a.has_shared) {
+      const uint32_t P = static_cast<uint32_t>(a.P);
+      for (uint32_t j = 0; j * ntl < static_cast<uint32_t>(a.T); ++j) {
+        RowTile t;
+        t.expert = static_cast<uint32_t>(E);
+        t.row_start = P + j * ntl;
+        t.rows = min(static_cast<uint32_t>(ntl), static_cast<uint32_t>(a.T) - j * ntl);
+        t.pad = 0;
+        rb.row_tiles[nrt++] = t;
+      }
+    }
+    *rb.n_row_tiles = nrt;
+    *rb.n_groups = grun;
+    // tiles of <= tile_expert_count groups, with the optional forced cut
+    const int ng = static_cast<int>(grun);
+    int nt = 0, gs = 0;
+    while (gs < ng) {
+      int ge = min(ng, gs + a.tile_expert_count);
+      if (a.tile_break >= 0 && gs < a.tile_break && ge > a.tile_break) ge = a.tile_break;
+      Tile t;
+      t.group_start = static_cast<uint32_t>(gs);
+      t.group_count = static_cast<uint32_t>(ge - gs);
+      const Group g0 = rb.groups[gs];
+      const Group g1 = rb.groups[ge - 1];
+      t.pair_start = g0.pair_start;
+      t.pair_count = g1.pair_start + g1.pair_count - g0.pair_start;
+      rb.tiles[nt++] = t;
+      gs = ge;
+    }
+    *rb.n_tiles = static_cast<uint32_t>(nt);
+  }
+}
+
+// ---- 3. stable scatter -----------------------------------------------------
+__global__ void __launch_bounds__(kThreads) permute_scatter_kernel(PermuteArgs a, RouteBuffers rb,
+                                                                  const uint16_t* tm_w16,
+                                                                  const float* w_f32) {
+  __shared__ uint32_t s_tmp[33];
+  const int e = blockIdx.x;
+  const uint32_t count = __ldcg(rb.counts + e);
+  if (count == 0u) return;
+  uint32_t run = __ldcg(rb.offsets + e);
+  for (int base = 0; base < a.P; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const bool hit = i < a.P && a.tm_ids[i] == static_cast<uint32_t>(e);
+    uint32_t tot;
+    const uint32_t pre = block_excl_scan(hit ? 1u : 0u, s_tmp, &tot);
+    if (hit) {
+      const uint32_t pos = run + pre;
+      Pair pr;
+      pr.token = static_cast<uint32_t>(i / a.K);
+      pr.expert = static_cast<uint32_t>(e);
+      pr.rank = static_cast<uint32_t>(i % a.K);
+      pr.weight_bits = tm_w16 ? tm_w16[i] : __half_as_ushort(__float2half_rn(w_f32[i]));
+      rb.sorted_pairs[pos] = pr;
+      rb.pair_pos[i] = pos;
+    }
+    run += tot;
+    if (run - __ldcg(rb.offsets + e) >= count) break;
+  }
+}
+
+__global__ void make_pairs_kernel(const uint32_t* ids, const uint16_t* w16, int T, int K,
+                                  Pair* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * K) return;
+  Pair p;
+  p.token = static_cast<uint32_t>(i / K);
+  p.expert = ids[i];
+  p.rank = static_cast<uint32_t>(i % K);
+  p.weight_bits = w16 ? w16[i] : 0u;
+  out[i] = p;
+}
+
+// ---- gather: sorted rows of the normalised input, as fp16 ------------------
+// Row i < n_rows takes token sorted_pairs[i].token; rows n_rows + t (when
+// append_tokens) take token t in order (the shared expert's input).  One warp
+// per row; also computes the raw shared-gate dot for the appended rows.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, uint32_t x_stride,
+                                                          const float* inv_rms,
+                                                          const Pair* sorted_pairs, int n_rows,
+                                                          int T, int D, int append_tokens,
+                                                          __half* xp, const float* gate_w,
+                                                          float* gate_raw) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total = n_rows + (append_tokens ? T : 0);
+  if (warp >= total) return;
+  const int t = warp < n_rows ? static_cast<int>(sorted_pairs[warp].token) : warp - n_rows;
+  if (t >= T) return;
+  const float inv = inv_rms[t];
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * x_stride);
+  uint4* dst = reinterpret_cast<uint4*>(xp + static_cast<size_t>(warp) * D);
+  const bool do_gate = warp >= n_rows && gate_w != nullptr;
+  float g = 0.0f;
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 v = __ldg(src + c);
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = __uint_as_float(wv[j] << 16);
+      const float b = __uint_as_float(wv[j] & 0xFFFF0000u);
+      if (do_gate) {
+        g = fmaf(gate_w[c * 8 + 2 * j], a, g);
+        g = fmaf(gate_w[c * 8 + 2 * j + 1], b, g);
+      }
+      __half2 h = __floats2half2_rn(a * inv, b * inv);
+      o[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (do_gate) {
+    g = warp_sum(g);
+    if (lane == 0) gate_raw[t] = g;
+  }
+}
+
+}  // namespace
+
+// Places caller-supplied pairs into token-major order (validating them) when
+// pairs_in is given; otherwise the router's ids/weights are already token
+// major.  Then counts, scans and scatters.
+cudaError_t launch_permute(const RouterParams& p, const RouteBuffers& rb, const Pair* pairs_in,
+                           cudaStream_t s) {
+  const int P = p.T * p.K;
+  if (P <= 0) return cudaSuccess;
+  const uint16_t* w16 = nullptr;
+  const uint32_t* tm_ids = rb.ids;
+  if (pairs_in) {
+    // ids / weights_f16 / pair_pos double as token-major scratch
+    uint32_t* occ = rb.pair_pos;
+    cudaError_t e = cudaMemsetAsync(occ, 0, sizeof(uint32_t) * P, s);
+    if (e != cudaSuccess) return e;
+    place_pairs_kernel<<<(P + 255) / 256, 256, 0, s>>>(pairs_in, P, p.T, p.K, p.E, rb.ids,
+                                                       rb.weights_f16, occ, rb.err);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    w16 = rb.weights_f16;
+  }
+  PermuteArgs a;
+  a.tm_ids = tm_ids;
+  a.T = p.T;
+  a.K = p.K;
+  a.E = p.E;
+  a.P = P;
+  a.tile_rows = p.tile_rows;
+  a.tile_expert_count = p.tile_expert_count;
+  a.tile_break = p.tile_break;
+  a.has_shared = p.has_shared;
+  a.sort_keys = p.sort_keys;
+  const size_t smem = 3u * p.E * sizeof(uint32_t);
+  permute_count_kernel<<<p.E, kThreads, smem, s>>>(a, rb);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  permute_scatter_kernel<<<p.E, kThreads, 0, s>>>(a, rb, w16, rb.weights);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_make_pairs(const uint32_t* ids, const uint16_t* w_f16, int T, int K, Pair* out,
+                              cudaStream_t s) {
+  const int n = T * K;
+  if (n <= 0) return cudaSuccess;
+  make_pairs_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, w_f16, T, K, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows_gate(const uint16_t* x, uint32_t x_stride, const float* inv_rms,
+                                    const Pair* sorted_pairs, int n_rows, int T, int D,
+                                    int append_tokens, __half* xp, const float* gate_w,
+                                    float* gate_raw, cudaStream_t s) {
+  const int total = n_rows + (append_tokens ? T : 0);
+  if (total <= 0) return cudaSuccess;
+  const int warps_per_cta = 8;
+  gather_rows_kernel<<<(total + warps_per_cta - 1) / warps_per_cta, 256, 0, s>>>(
+      x, x_stride, inv_rms, sorted_pairs, n_rows, T, D, append_tokens, xp, gate_w, gate_raw);
+  return cudaGetLastError();
+}
+
+
+}  // namespace tsg

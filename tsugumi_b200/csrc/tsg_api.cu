@@ -1,0 +1,905 @@
+// tsg_api.cu -- the C ABI of libtsugumi_cuda.so (include/tsugumi_cuda.h).
+//
+// Host-side mirror of the reference's encoder classes: a context plays the
+// part of MetalContext plus the kernel objects' owned scratch
+// (MoE.swift:184-198 router logits and argument buffer), a layer holds the
+// resident weights the Swift runners keep per layer.  Every entry point
+// validates its arguments the way the reference's preconditions and throws
+// do, then enqueues kernels on the context's stream.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/tsugumi_cuda.h"
+#include "tsg_common.cuh"
+#include "tsg_kernels.cuh"
+
+using namespace tsg;
+
+namespace {
+
+// Workspace capacity in elements of each dimension.
+struct Caps {
+  uint32_t T = 0, D = 0, F = 0, E = 0, K = 0;
+  bool covers(const Caps& o) const {
+    return T >= o.T && D >= o.D && F >= o.F && E >= o.E && K >= o.K;
+  }
+  Caps max_with(const Caps& o) const {
+    Caps c;
+    c.T = std::max(T, o.T);
+    c.D = std::max(D, o.D);
+    c.F = std::max(F, o.F);
+    c.E = std::max(E, o.E);
+    c.K = std::max(K, o.K);
+    return c;
+  }
+};
+
+constexpr int kMaxSplit = 8;
+
+}  // namespace
+
+struct tsg_ctx_s {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  uint32_t decode_max_tokens = 64;
+  std::string last_error;
+  // workspace
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  Caps caps;
+  RouteBuffers rb{};
+  __half* act_buf = nullptr;
+  __half* xp = nullptr;
+  __half* partials = nullptr;
+  // device status words: [0] error bits, [1] code, [2] value, [3] pad;
+  // [4] last-CTA counter
+  uint32_t* status = nullptr;
+  // last call's routing
+  uint32_t last_T = 0, last_K = 0;
+  // stage profiling: 5 events per recorded call
+  std::vector<cudaEvent_t> prof_events;
+  uint32_t prof_max = 0, prof_calls = 0;
+  bool profiling = false;
+};
+
+struct tsg_moe_layer_s {
+  tsg_ctx ctx = nullptr;
+  tsg_moe_layer_desc desc{};
+  float* router_rows = nullptr;  // [E + has_gate][D], owned
+  int has_gate = 0;
+  int has_shared = 0;
+};
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+tsg_status fail(tsg_ctx ctx, tsg_status st, const std::string& msg) {
+  if (ctx) ctx->last_error = msg;
+  return st;
+}
+
+tsg_status cuda_fail(tsg_ctx ctx, cudaError_t e, const char* where) {
+  return fail(ctx, e == cudaErrorMemoryAllocation ? TSG_ERR_OOM : TSG_ERR_CUDA,
+              std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+#define TSG_CUDA_TRY(ctx, expr, where)                 \
+  do {                                                 \
+    cudaError_t e__ = (expr);                          \
+    if (e__ != cudaSuccess) return cuda_fail(ctx, e__, where); \
+  } while (0)
+
+// Rows a prefill schedule can need: one tile per tile_rows routed rows plus
+// one partial tile per expert, plus the shared expert's tiles.
+uint32_t max_row_tiles(uint32_t T, uint32_t K, uint32_t E, uint32_t tile_rows) {
+  return (T * K + tile_rows - 1) / tile_rows + E + (T + tile_rows - 1) / tile_rows + 1;
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Carves the workspace; with base == nullptr only returns the size.
+size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> void* {
+    off = align_up(off, 256);
+    void* p = base ? base + off : nullptr;
+    off += bytes;
+    return p;
+  };
+  const size_t T = c.T, D = c.D, F = c.F, E = c.E, K = c.K;
+  const size_t P = T * K;
+  const size_t rows = P + T;
+  RouteBuffers rb{};
+  rb.logits_raw = static_cast<float*>(take(kMaxSplit * T * E * 4));
+  rb.gate_raw = static_cast<float*>(take(T * 4));
+  rb.sumsq = static_cast<float*>(take(kMaxSplit * T * 4));
+  rb.inv_rms = static_cast<float*>(take(T * 4));
+  rb.ids = static_cast<uint32_t*>(take(P * 4));
+  rb.weights = static_cast<float*>(take(P * 4));
+  rb.weights_f16 = static_cast<uint16_t*>(take(P * 2));
+  rb.counts = static_cast<uint32_t*>(take(E * 4));
+  rb.offsets = static_cast<uint32_t*>(take(E * 4));
+  rb.sorted_pairs = static_cast<Pair*>(take(P * sizeof(Pair)));
+  rb.pair_pos = static_cast<uint32_t*>(take(P * 4));
+  rb.groups = static_cast<Group*>(take(E * sizeof(Group)));
+  rb.n_groups = static_cast<uint32_t*>(take(4));
+  rb.tiles = static_cast<Tile*>(take(E * sizeof(Tile)));
+  rb.n_tiles = static_cast<uint32_t*>(take(4));
+  const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
+  rb.row_tiles = static_cast<RowTile*>(
+      take(max_row_tiles(static_cast<uint32_t>(T), static_cast<uint32_t>(K),
+                         static_cast<uint32_t>(E), tr) * sizeof(RowTile)));
+  rb.n_row_tiles = static_cast<uint32_t*>(take(4));
+  const size_t Td = std::min<size_t>(T, 64);
+  rb.xn = static_cast<float*>(take(Td * D * 4));
+  rb.xs8 = static_cast<float*>(take(Td * (D / 8) * 4));
+  __half* act = static_cast<__half*>(take(rows * F * 2));
+  __half* xp = static_cast<__half*>(take(rows * D * 2));
+  __half* part = static_cast<__half*>(take(rows * D * 2));
+  if (base) {
+    rb.sync_counter = ctx->status + 4;
+    rb.err = ctx->status;
+    ctx->rb = rb;
+    ctx->act_buf = act;
+    ctx->xp = xp;
+    ctx->partials = part;
+  }
+  return align_up(off, 256);
+}
+
+tsg_status ensure_workspace(tsg_ctx ctx, const Caps& want) {
+  if (ctx->ws && ctx->caps.covers(want)) return TSG_OK;
+  const Caps c = ctx->caps.max_with(want);
+  const size_t bytes = carve(ctx, c, nullptr);
+  TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  if (ctx->ws) {
+    TSG_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+  }
+  void* p = nullptr;
+  TSG_CUDA_TRY(ctx, cudaMalloc(&p, bytes), "cudaMalloc(workspace)");
+  ctx->ws = p;
+  ctx->ws_bytes = bytes;
+  ctx->caps = c;
+  carve(ctx, c, static_cast<uint8_t*>(p));
+  return TSG_OK;
+}
+
+Caps layer_caps(const tsg_moe_layer_s* L, uint32_t T) {
+  Caps c;
+  c.T = T;
+  c.D = L->desc.d;
+  c.F = L->desc.f;
+  c.E = L->desc.num_experts;
+  c.K = std::max<uint32_t>(L->desc.top_k, 1);
+  return c;
+}
+
+RouterParams router_params(const tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
+                           uint32_t T) {
+  RouterParams p{};
+  p.x = static_cast<const uint16_t*>(x);
+  p.x_stride = x_stride;
+  p.T = static_cast<int>(T);
+  p.D = static_cast<int>(L->desc.d);
+  p.E = static_cast<int>(L->desc.num_experts);
+  p.K = static_cast<int>(L->desc.top_k);
+  p.w = L->router_rows;
+  p.has_gate = L->has_gate;
+  p.has_shared = L->has_shared;
+  p.per_expert_scale = L->desc.per_expert_scale;
+  p.logit_bias = L->desc.logit_bias;
+  p.norm = L->desc.router_norm ? 1 : 0;
+  p.eps = L->desc.norm_eps;
+  p.tile_rows = qmm_tile_rows();
+  p.tile_expert_count = 16;
+  p.tile_break = -1;
+  p.sort_keys = nullptr;
+  return p;
+}
+
+ExpertSet expert_set(const tsg_moe_layer_s* L) {
+  ExpertSet s{};
+  s.base = static_cast<const uint8_t*>(L->desc.experts);
+  s.stride = L->desc.expert_stride;
+  std::memcpy(&s.off, &L->desc.offsets, sizeof(ExpertOffsets));
+  s.shared = static_cast<const uint8_t*>(L->desc.shared_expert);
+  std::memcpy(&s.shared_off, &L->desc.shared_offsets, sizeof(ExpertOffsets));
+  return s;
+}
+
+bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, 16};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Records stage boundary `k` (0..4) of the current profiled call.
+void prof_mark(tsg_ctx ctx, int k) {
+  if (!ctx->profiling || ctx->prof_calls >= ctx->prof_max) return;
+  cudaEventRecord(ctx->prof_events[ctx->prof_calls * 5 + k], ctx->stream);
+}
+
+bool valid_dtype(tsg_dtype t) { return t == TSG_DTYPE_BF16 || t == TSG_DTYPE_F32; }
+
+// ---- the two regimes ----
+
+tsg_status run_decode_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
+                              uint32_t T, const float* residual, void* y, uint32_t y_stride,
+                              tsg_dtype y_dtype) {
+  DecodeParams dp{};
+  dp.T = static_cast<int>(T);
+  dp.D = static_cast<int>(L->desc.d);
+  dp.F = static_cast<int>(L->desc.f);
+  dp.E = static_cast<int>(L->desc.num_experts);
+  dp.K = static_cast<int>(L->desc.top_k);
+  dp.act = static_cast<int>(L->desc.activation);
+  dp.has_shared = L->has_shared;
+  dp.x = static_cast<const uint16_t*>(x);
+  dp.x_stride = x_stride;
+  dp.experts = expert_set(L);
+  dp.rb = ctx->rb;
+  if (!L->has_gate) dp.rb.gate_raw = nullptr;
+  dp.act_buf = ctx->act_buf;
+  dp.xn = ctx->rb.xn;
+  dp.xs8 = ctx->rb.xs8;
+  dp.y = y;
+  dp.y_stride = y_stride;
+  dp.y_f32 = y_dtype == TSG_DTYPE_F32 ? 1 : 0;
+  dp.residual = residual;
+  dp.num_sms = ctx->num_sms;
+  TSG_CUDA_TRY(ctx, launch_decode_gate_up(dp, ctx->stream), "decode gate/up");
+  prof_mark(ctx, 2);
+  TSG_CUDA_TRY(ctx, launch_decode_down(dp, ctx->stream), "decode down");
+  prof_mark(ctx, 3);
+  prof_mark(ctx, 4);
+  return TSG_OK;
+}
+
+tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
+                               uint32_t T, const float* residual, void* y, uint32_t y_stride,
+                               tsg_dtype y_dtype) {
+  // assumes rb.ids / rb.weights / rb.inv_rms are filled for T tokens
+  const RouterParams rp = router_params(L, x, x_stride, T);
+  const uint32_t K = L->desc.top_k;
+  const uint32_t P = T * K;
+  TSG_CUDA_TRY(ctx, launch_permute(rp, ctx->rb, nullptr, ctx->stream), "permute");
+  const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(L->desc.num_experts) * L->desc.d
+                                    : nullptr;
+  TSG_CUDA_TRY(ctx,
+               launch_gather_rows_gate(static_cast<const uint16_t*>(x), x_stride, ctx->rb.inv_rms,
+                                       ctx->rb.sorted_pairs, static_cast<int>(P),
+                                       static_cast<int>(T), static_cast<int>(L->desc.d),
+                                       L->has_shared, ctx->xp, gate_w, ctx->rb.gate_raw,
+                                       ctx->stream),
+               "gather rows");
+  const uint32_t rows = P + (L->has_shared ? T : 0u);
+  CUtensorMap maps[2];
+  if (!encode_rows_map(&maps[0], ctx->xp, rows, L->desc.d) ||
+      !encode_rows_map(&maps[1], ctx->act_buf, rows, L->desc.f))
+    return fail(ctx, TSG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  QmmParams qp{};
+  qp.D = static_cast<int>(L->desc.d);
+  qp.F = static_cast<int>(L->desc.f);
+  qp.E = static_cast<int>(L->desc.num_experts);
+  qp.act = static_cast<int>(L->desc.activation);
+  qp.n_rows_total = static_cast<int>(rows);
+  qp.experts = expert_set(L);
+  qp.row_tiles = ctx->rb.row_tiles;
+  qp.n_row_tiles = ctx->rb.n_row_tiles;
+  qp.xp = ctx->xp;
+  qp.act_buf = ctx->act_buf;
+  qp.partials = ctx->partials;
+  qp.err = ctx->rb.err;
+  qp.num_sms = ctx->num_sms;
+  qp.maps = maps;
+  prof_mark(ctx, 1);
+  TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, ctx->stream), "qmm gate/up");
+  prof_mark(ctx, 2);
+  TSG_CUDA_TRY(ctx, launch_qmm_down(qp, ctx->stream), "qmm down");
+  prof_mark(ctx, 3);
+  CombineParams cp{};
+  cp.T = static_cast<int>(T);
+  cp.D = static_cast<int>(L->desc.d);
+  cp.K = static_cast<int>(K);
+  cp.has_shared = L->has_shared;
+  cp.E = static_cast<int>(L->desc.num_experts);
+  cp.partials = ctx->partials;
+  cp.pair_pos = ctx->rb.pair_pos;
+  cp.weights = ctx->rb.weights;
+  cp.gate_raw = L->has_gate ? ctx->rb.gate_raw : nullptr;
+  cp.inv_rms = ctx->rb.inv_rms;
+  cp.residual = residual;
+  cp.y = y;
+  cp.y_stride = y_stride;
+  cp.y_f32 = y_dtype == TSG_DTYPE_F32 ? 1 : 0;
+  TSG_CUDA_TRY(ctx, launch_combine(cp, ctx->stream), "combine");
+  prof_mark(ctx, 4);
+  return TSG_OK;
+}
+
+tsg_status check_common(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32_t x_stride,
+                        uint32_t T, const void* y, uint32_t y_stride, tsg_dtype y_dtype) {
+  if (!ctx || !L) return fail(ctx, TSG_ERR_INVALID_ARG, "null context or layer");
+  if (L->ctx != ctx) return fail(ctx, TSG_ERR_INVALID_ARG, "layer belongs to another context");
+  if (T == 0) return TSG_OK;
+  if (!x || !y) return fail(ctx, TSG_ERR_INVALID_ARG, "null input or output");
+  if (x_stride < L->desc.d || x_stride % 8)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "hidden stride is too small or not a multiple of 8");
+  if (y_stride < L->desc.d || y_stride % 8)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "output stride is too small or not a multiple of 8");
+  if (!valid_dtype(y_dtype)) return fail(ctx, TSG_ERR_INVALID_ARG, "output dtype must be bf16 or f32");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "input and output must be 16-byte aligned");
+  return TSG_OK;
+}
+
+const char* grouping_error_text(uint32_t code) {
+  switch (code) {
+    case 6: return "route token %u is out of range";
+    case 7: return "route rank %u is out of range";
+    case 8: return "route expert %u is out of range";
+    case 9: return "duplicate route pair for token %u";
+    default: return "routing metadata failed validation (value %u)";
+  }
+}
+
+__global__ void fold_router_kernel(const float* w, const float* eff, const float* gate, int E,
+                                   int D, float* out) {
+  const size_t n = static_cast<size_t>(E) * D;
+  for (size_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n + (gate ? D : 0);
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    if (i < n) {
+      const float s = eff ? eff[i % D] : 1.0f;
+      out[i] = w[i] * s;
+    } else {
+      out[i] = gate[i - n];
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int tsg_abi_version(void) { return TSG_ABI_VERSION; }
+
+tsg_status tsg_ctx_create(int device, void* stream, tsg_ctx* out) {
+  if (!out) return TSG_ERR_INVALID_ARG;
+  *out = nullptr;
+  tsg_ctx ctx = new (std::nothrow) tsg_ctx_s();
+  if (!ctx) return TSG_ERR_OOM;
+  ctx->device = device;
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+  int major = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e == cudaSuccess && major != 10) {
+    delete ctx;
+    return TSG_ERR_UNSUPPORTED_SHAPE;  // sm_100a only
+  }
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->status, 8 * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, 8 * sizeof(uint32_t));
+  if (e != cudaSuccess) {
+    delete ctx;
+    return e == cudaErrorMemoryAllocation ? TSG_ERR_OOM : TSG_ERR_CUDA;
+  }
+  *out = ctx;
+  return TSG_OK;
+}
+
+tsg_status tsg_ctx_destroy(tsg_ctx ctx) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->status) cudaFree(ctx->status);
+  for (cudaEvent_t e : ctx->prof_events) cudaEventDestroy(e);
+  delete ctx;
+  return TSG_OK;
+}
+
+tsg_status tsg_ctx_set_stream(tsg_ctx ctx, void* stream) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  return TSG_OK;
+}
+
+tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  if (t > 64) return fail(ctx, TSG_ERR_INVALID_ARG, "decode regime handles at most 64 tokens");
+  ctx->decode_max_tokens = t;
+  return TSG_OK;
+}
+
+tsg_status tsg_ctx_reserve(tsg_ctx ctx, tsg_moe_layer layer, uint32_t max_tokens) {
+  if (!ctx || !layer) return fail(ctx, TSG_ERR_INVALID_ARG, "null context or layer");
+  return ensure_workspace(ctx, layer_caps(layer, max_tokens));
+}
+
+tsg_status tsg_sync(tsg_ctx ctx) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  cudaSetDevice(ctx->device);
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "stream");
+  uint32_t st[3] = {0, 0, 0};
+  e = cudaMemcpy(st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "status readback");
+  if (st[0] == 0u) return TSG_OK;
+  cudaMemset(ctx->status, 0, 4 * sizeof(uint32_t));
+  if (st[0] & TSG_DEVERR_TIMEOUT) {
+    return fail(ctx, TSG_ERR_TIMEOUT, "a device-side wait ran out of time (pipeline fault)");
+  }
+  char buf[160];
+  std::snprintf(buf, sizeof(buf), grouping_error_text(st[1]), st[2]);
+  return fail(ctx, TSG_ERR_METADATA, buf);
+}
+
+const char* tsg_last_error_string(tsg_ctx ctx) {
+  return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc* d, tsg_moe_layer* out) {
+  if (!ctx || !d || !out) return fail(ctx, TSG_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (d->group_size != 32) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "group size must be 32");
+  if (d->d == 0 || d->d % 256) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "D must be a multiple of 256");
+  if (d->f == 0 || d->f % 64) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "F must be a multiple of 64");
+  if (d->num_experts == 0 || d->num_experts > 512)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "numExperts must be in 1...512");
+  if (d->top_k == 0 || d->top_k > 32 || d->top_k > d->num_experts)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "topK must be in 1...min(32, numExperts)");
+  if (d->activation != TSG_ACT_GELU_PYTORCH_TANH && d->activation != TSG_ACT_SILU)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "unknown gate activation");
+  if (!d->experts || !d->router_weight) return fail(ctx, TSG_ERR_INVALID_ARG, "null experts or router");
+  const tsg_expert_offsets& o = d->offsets;
+  const uint64_t align_bits = reinterpret_cast<uintptr_t>(d->experts) | d->expert_stride |
+                              o.gate_w_off | o.gate_s_off | o.up_w_off | o.up_s_off |
+                              o.down_w_off | o.down_s_off;
+  if (align_bits & 15u)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "expert blobs and sub-tensors must be 16-byte aligned");
+  if (d->shared_expert) {
+    if (d->shared_f != d->f) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "shared F must equal F");
+    const tsg_expert_offsets& so = d->shared_offsets;
+    const uint64_t sb = reinterpret_cast<uintptr_t>(d->shared_expert) | so.gate_w_off |
+                        so.gate_s_off | so.up_w_off | so.up_s_off | so.down_w_off | so.down_s_off;
+    if (sb & 15u) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "shared expert must be 16-byte aligned");
+  }
+  tsg_moe_layer L = new (std::nothrow) tsg_moe_layer_s();
+  if (!L) return fail(ctx, TSG_ERR_OOM, "layer");
+  L->ctx = ctx;
+  L->desc = *d;
+  L->has_shared = d->shared_expert ? 1 : 0;
+  L->has_gate = (d->shared_expert && d->shared_gate) ? 1 : 0;
+  const size_t rows = d->num_experts + (L->has_gate ? 1 : 0);
+  cudaError_t e = cudaSetDevice(ctx->device);
+  if (e == cudaSuccess) e = cudaMalloc(&L->router_rows, rows * d->d * sizeof(float));
+  if (e == cudaSuccess) {
+    fold_router_kernel<<<256, 256, 0, ctx->stream>>>(d->router_weight, d->effective_scale,
+                                                     L->has_gate ? d->shared_gate : nullptr,
+                                                     static_cast<int>(d->num_experts),
+                                                     static_cast<int>(d->d), L->router_rows);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    if (L->router_rows) cudaFree(L->router_rows);
+    delete L;
+    return cuda_fail(ctx, e, "layer create");
+  }
+  *out = L;
+  return TSG_OK;
+}
+
+tsg_status tsg_moe_layer_destroy(tsg_moe_layer L) {
+  if (!L) return TSG_ERR_INVALID_ARG;
+  if (L->ctx) cudaStreamSynchronize(L->ctx->stream);
+  if (L->router_rows) cudaFree(L->router_rows);
+  delete L;
+  return TSG_OK;
+}
+
+tsg_status tsg_router_topk(tsg_ctx ctx, tsg_moe_layer L, const void* hidden, uint32_t hidden_stride,
+                           uint32_t T, uint32_t* out_indices, float* out_weights,
+                           uint16_t* out_weights_f16) {
+  if (!ctx || !L) return fail(ctx, TSG_ERR_INVALID_ARG, "null context or layer");
+  if (T == 0) return TSG_OK;
+  if (!hidden || !out_indices || !out_weights) return fail(ctx, TSG_ERR_INVALID_ARG, "null buffer");
+  if (hidden_stride < L->desc.d || hidden_stride % 8)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "hidden stride is too small");
+  tsg_status st = ensure_workspace(ctx, layer_caps(L, T));
+  if (st != TSG_OK) return st;
+  RouterParams p = router_params(L, hidden, hidden_stride, T);
+  RouteBuffers rb = ctx->rb;
+  rb.ids = out_indices;
+  rb.weights = out_weights;
+  rb.weights_f16 = out_weights_f16;
+  if (T <= ctx->decode_max_tokens) {
+    TSG_CUDA_TRY(ctx, launch_router_decode(p, rb, ctx->stream), "router (decode)");
+  } else {
+    TSG_CUDA_TRY(ctx, launch_router_prefill(p, rb, ctx->stream), "router (prefill)");
+  }
+  return TSG_OK;
+}
+
+tsg_status tsg_make_token_expert_pairs(tsg_ctx ctx, const uint32_t* indices,
+                                       const uint16_t* weights_f16, uint32_t T, uint32_t K,
+                                       tsg_token_expert_pair* out) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  if (T * K == 0) return TSG_OK;
+  if (!indices || !out) return fail(ctx, TSG_ERR_INVALID_ARG, "null buffer");
+  TSG_CUDA_TRY(ctx,
+               launch_make_pairs(indices, weights_f16, static_cast<int>(T), static_cast<int>(K),
+                                 reinterpret_cast<Pair*>(out), ctx->stream),
+               "make pairs");
+  return TSG_OK;
+}
+
+tsg_status tsg_moe_group_pairs(tsg_ctx ctx, const tsg_token_expert_pair* pairs, uint32_t n_pairs,
+                               int32_t query_count, int32_t top_k, int32_t num_experts,
+                               int32_t tile_expert_count, const uint64_t* sort_keys,
+                               int32_t n_sort_keys, int32_t tile_break,
+                               tsg_token_expert_pair* sorted_pairs, uint32_t* offsets,
+                               uint32_t* counts, tsg_moe_group* groups, uint32_t* n_groups,
+                               tsg_moe_tile* tiles, uint32_t* n_tiles) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  char buf[128];
+  // argument checks in the order of PrefillMoEGrouping.swift:100-120
+  if (query_count < 0) {
+    std::snprintf(buf, sizeof(buf), "queryCount must be non-negative, got %d", query_count);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (top_k <= 0) {
+    std::snprintf(buf, sizeof(buf), "topK must be positive, got %d", top_k);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (num_experts <= 0) {
+    std::snprintf(buf, sizeof(buf), "numExperts must be positive, got %d", num_experts);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (tile_expert_count < 1 || tile_expert_count > 16) {
+    std::snprintf(buf, sizeof(buf), "tileExpertCount must be in 1...16, got %d", tile_expert_count);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (sort_keys && n_sort_keys != num_experts) {
+    std::snprintf(buf, sizeof(buf), "expected %d expert sort keys, got %d", num_experts, n_sort_keys);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  const uint64_t expected = static_cast<uint64_t>(query_count) * static_cast<uint64_t>(top_k);
+  if (n_pairs != expected) {
+    std::snprintf(buf, sizeof(buf), "expected %llu route pairs, got %u",
+                  static_cast<unsigned long long>(expected), n_pairs);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (num_experts > 512) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "numExperts > 512");
+  if (n_pairs > 0 && (!pairs || !sorted_pairs)) return fail(ctx, TSG_ERR_INVALID_ARG, "null pairs");
+  if (!offsets || !counts || !groups || !n_groups || !tiles || !n_tiles)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "null output");
+  Caps c;
+  c.T = static_cast<uint32_t>(query_count);
+  c.K = static_cast<uint32_t>(top_k);
+  c.E = static_cast<uint32_t>(num_experts);
+  c.D = 256;
+  c.F = 64;
+  tsg_status st = ensure_workspace(ctx, c);
+  if (st != TSG_OK) return st;
+  RouterParams p{};
+  p.T = query_count;
+  p.K = top_k;
+  p.E = num_experts;
+  p.tile_rows = qmm_tile_rows();
+  p.tile_expert_count = tile_expert_count;
+  p.tile_break = tile_break;
+  p.sort_keys = sort_keys;
+  RouteBuffers rb = ctx->rb;
+  rb.sorted_pairs = reinterpret_cast<Pair*>(sorted_pairs);
+  rb.offsets = offsets;
+  rb.counts = counts;
+  rb.groups = reinterpret_cast<Group*>(groups);
+  rb.n_groups = n_groups;
+  rb.tiles = reinterpret_cast<Tile*>(tiles);
+  rb.n_tiles = n_tiles;
+  if (n_pairs == 0) {
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(offsets, 0xFF, num_experts * 4u, ctx->stream), "memset");
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(counts, 0, num_experts * 4u, ctx->stream), "memset");
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(n_groups, 0, 4, ctx->stream), "memset");
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(n_tiles, 0, 4, ctx->stream), "memset");
+    return TSG_OK;
+  }
+  TSG_CUDA_TRY(ctx, launch_permute(p, rb, reinterpret_cast<const Pair*>(pairs), ctx->stream),
+               "group pairs");
+  return TSG_OK;
+}
+
+tsg_status tsg_plan_routed_gemm(const tsg_moe_group* groups, uint32_t n_groups,
+                                uint32_t max_rows_per_batch, uint32_t tile_rows,
+                                tsg_routed_gemm_block* blocks, uint32_t max_blocks,
+                                uint32_t* n_blocks, uint32_t* batch_rows,
+                                uint32_t* batch_first_block, uint32_t* batch_block_count,
+                                uint32_t max_batches, uint32_t* n_batches) {
+  if ((n_groups && !groups) || !n_blocks || !n_batches || tile_rows == 0) return TSG_ERR_INVALID_ARG;
+  uint32_t budget = (max_rows_per_batch / tile_rows) * tile_rows;
+  if (budget < tile_rows) budget = tile_rows;
+  uint32_t nb = 0, nbatch = 0, rows = 0, first = 0;
+  bool overflow = false;
+  auto flush = [&]() {
+    if (rows == 0) return;
+    if (nbatch < max_batches) {
+      batch_rows[nbatch] = rows;
+      batch_first_block[nbatch] = first;
+      batch_block_count[nbatch] = nb - first;
+    } else {
+      overflow = true;
+    }
+    ++nbatch;
+    first = nb;
+    rows = 0;
+  };
+  for (uint32_t slot = 0; slot < n_groups; ++slot) {
+    uint32_t taken = 0;
+    const uint32_t count = groups[slot].pair_count;
+    while (taken < count) {
+      if (rows == budget) flush();
+      if (rows > 0 && rows + (count - taken) > budget) flush();  // never split a group that fits
+      const uint32_t take = std::min(count - taken, budget - rows);
+      uint32_t done = 0;
+      while (done < take) {
+        const uint32_t rc = std::min(tile_rows, take - done);
+        if (nb < max_blocks) {
+          blocks[nb].local_slot = slot;
+          blocks[nb].pair_start = groups[slot].pair_start + taken + done;
+          blocks[nb].row_count = rc;
+          blocks[nb].local_row = rows + done;
+        } else {
+          overflow = true;
+        }
+        ++nb;
+        done += rc;
+      }
+      rows += take;
+      taken += take;
+    }
+  }
+  flush();
+  *n_blocks = nb;
+  *n_batches = nbatch;
+  return overflow ? TSG_ERR_INVALID_ARG : TSG_OK;
+}
+
+tsg_status tsg_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
+                                 uint32_t hidden_stride, uint32_t T, const float* residual,
+                                 void* y, uint32_t y_stride, tsg_dtype y_dtype) {
+  tsg_status st = check_common(ctx, L, hidden, hidden_stride, T, y, y_stride, y_dtype);
+  if (st != TSG_OK || T == 0) return st;
+  st = ensure_workspace(ctx, layer_caps(L, T));
+  if (st != TSG_OK) return st;
+  RouterParams p = router_params(L, hidden, hidden_stride, T);
+  ctx->last_T = T;
+  ctx->last_K = L->desc.top_k;
+  prof_mark(ctx, 0);
+  tsg_status r;
+  if (T <= ctx->decode_max_tokens) {
+    TSG_CUDA_TRY(ctx, launch_router_decode(p, ctx->rb, ctx->stream), "router (decode)");
+    prof_mark(ctx, 1);
+    r = run_decode_experts(ctx, L, hidden, hidden_stride, T, residual, y, y_stride, y_dtype);
+  } else {
+    TSG_CUDA_TRY(ctx, launch_router_prefill(p, ctx->rb, ctx->stream), "router (prefill)");
+    r = run_prefill_experts(ctx, L, hidden, hidden_stride, T, residual, y, y_stride, y_dtype);
+  }
+  if (ctx->profiling && ctx->prof_calls < ctx->prof_max) ++ctx->prof_calls;
+  return r;
+}
+
+tsg_status tsg_ctx_profile_begin(tsg_ctx ctx, uint32_t max_calls) {
+  if (!ctx || max_calls == 0) return fail(ctx, TSG_ERR_INVALID_ARG, "max_calls must be positive");
+  cudaSetDevice(ctx->device);
+  for (cudaEvent_t e : ctx->prof_events) cudaEventDestroy(e);
+  ctx->prof_events.assign(static_cast<size_t>(max_calls) * 5, nullptr);
+  for (auto& e : ctx->prof_events) TSG_CUDA_TRY(ctx, cudaEventCreate(&e), "cudaEventCreate");
+  ctx->prof_max = max_calls;
+  ctx->prof_calls = 0;
+  ctx->profiling = true;
+  return TSG_OK;
+}
+
+tsg_status tsg_ctx_profile_end(tsg_ctx ctx, float* stage_ms, uint32_t* n_calls) {
+  if (!ctx || !stage_ms) return fail(ctx, TSG_ERR_INVALID_ARG, "null argument");
+  ctx->profiling = false;
+  TSG_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "stream");
+  for (int k = 0; k < 4; ++k) stage_ms[k] = 0.0f;
+  for (uint32_t c = 0; c < ctx->prof_calls; ++c) {
+    for (int k = 0; k < 4; ++k) {
+      float ms = 0.0f;
+      TSG_CUDA_TRY(ctx, cudaEventElapsedTime(&ms, ctx->prof_events[c * 5 + k],
+                                             ctx->prof_events[c * 5 + k + 1]),
+                   "cudaEventElapsedTime");
+      stage_ms[k] += ms;
+    }
+  }
+  if (n_calls) *n_calls = ctx->prof_calls;
+  return TSG_OK;
+}
+
+static tsg_status experts_with_routing(tsg_ctx ctx, tsg_moe_layer L, const void* x,
+                                       uint32_t x_stride, uint32_t T, const uint32_t* indices,
+                                       const float* weights, const float* residual, void* y,
+                                       uint32_t y_stride, tsg_dtype y_dtype, bool decode) {
+  tsg_status st = check_common(ctx, L, x, x_stride, T, y, y_stride, y_dtype);
+  if (st != TSG_OK || T == 0) return st;
+  if (!indices || !weights) return fail(ctx, TSG_ERR_INVALID_ARG, "null routing");
+  if (decode && T > 64) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "decode regime takes at most 64 tokens");
+  st = ensure_workspace(ctx, layer_caps(L, T));
+  if (st != TSG_OK) return st;
+  const size_t P = static_cast<size_t>(T) * L->desc.top_k;
+  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->rb.ids, indices, P * 4, cudaMemcpyDeviceToDevice, ctx->stream),
+               "copy ids");
+  TSG_CUDA_TRY(ctx,
+               cudaMemcpyAsync(ctx->rb.weights, weights, P * 4, cudaMemcpyDeviceToDevice, ctx->stream),
+               "copy weights");
+  RouterParams p = router_params(L, x, x_stride, T);
+  ctx->last_T = T;
+  ctx->last_K = L->desc.top_k;
+  TSG_CUDA_TRY(ctx, launch_rowprep(p, ctx->rb, decode ? 1 : 0, ctx->stream), "row prep");
+  if (decode) {
+    TSG_CUDA_TRY(ctx, launch_group_small(p, ctx->rb, ctx->stream), "group");
+    return run_decode_experts(ctx, L, x, x_stride, T, residual, y, y_stride, y_dtype);
+  }
+  return run_prefill_experts(ctx, L, x, x_stride, T, residual, y, y_stride, y_dtype);
+}
+
+tsg_status tsg_moe_experts_decode(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32_t x_stride,
+                                  uint32_t T, const uint32_t* indices, const float* weights,
+                                  const float* residual, void* y, uint32_t y_stride,
+                                  tsg_dtype y_dtype) {
+  return experts_with_routing(ctx, L, x, x_stride, T, indices, weights, residual, y, y_stride,
+                              y_dtype, true);
+}
+
+tsg_status tsg_moe_experts_prefill(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32_t x_stride,
+                                   uint32_t T, const uint32_t* indices, const float* weights,
+                                   const float* residual, void* y, uint32_t y_stride,
+                                   tsg_dtype y_dtype) {
+  return experts_with_routing(ctx, L, x, x_stride, T, indices, weights, residual, y, y_stride,
+                              y_dtype, false);
+}
+
+tsg_status tsg_moe_reduce_token_major(tsg_ctx ctx, const uint16_t* partials, const float* weights,
+                                      uint32_t T, uint32_t K, uint32_t D, void* h2,
+                                      tsg_dtype h2_dtype) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  if (T == 0) return TSG_OK;
+  if (!partials || !weights || !h2) return fail(ctx, TSG_ERR_INVALID_ARG, "null buffer");
+  if (h2_dtype != TSG_DTYPE_F32 && h2_dtype != TSG_DTYPE_F16)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "h2 dtype must be f16 or f32");
+  TSG_CUDA_TRY(ctx,
+               launch_reduce_token_major(reinterpret_cast<const __half*>(partials), weights,
+                                         static_cast<int>(T), static_cast<int>(K),
+                                         static_cast<int>(D), h2, h2_dtype == TSG_DTYPE_F32,
+                                         ctx->stream),
+               "reduce token major");
+  return TSG_OK;
+}
+
+tsg_status tsg_shared_expert(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32_t x_stride,
+                             uint32_t T, void* y, uint32_t y_stride, tsg_dtype y_dtype) {
+  tsg_status st = check_common(ctx, L, x, x_stride, T, y, y_stride, y_dtype);
+  if (st != TSG_OK || T == 0) return st;
+  if (!L->has_shared) return fail(ctx, TSG_ERR_INVALID_ARG, "layer has no shared expert");
+  st = ensure_workspace(ctx, layer_caps(L, T));
+  if (st != TSG_OK) return st;
+  // a view of the layer with no routed slots: the schedule holds only the
+  // shared expert's row tiles
+  tsg_moe_layer_s V = *L;
+  V.desc.top_k = 0;
+  RouterParams p = router_params(&V, x, x_stride, T);
+  TSG_CUDA_TRY(ctx, launch_rowprep(p, ctx->rb, 0, ctx->stream), "row prep");
+  RouteBuffers rb = ctx->rb;
+  TSG_CUDA_TRY(ctx, cudaMemsetAsync(rb.n_groups, 0, 4, ctx->stream), "memset");
+  // shared-only schedule: T rows appended after zero routed rows
+  const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
+  const uint32_t ntile = (T + tr - 1) / tr;
+  RowTile host_tiles[64];
+  if (ntile > 64) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "shared expert call limited to 8192 tokens");
+  for (uint32_t j = 0; j < ntile; ++j) {
+    host_tiles[j].expert = L->desc.num_experts;
+    host_tiles[j].row_start = j * tr;
+    host_tiles[j].rows = std::min(tr, T - j * tr);
+    host_tiles[j].pad = 0;
+  }
+  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(rb.row_tiles, host_tiles, ntile * sizeof(RowTile),
+                                    cudaMemcpyHostToDevice, ctx->stream), "tiles");
+  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(rb.n_row_tiles, &ntile, 4, cudaMemcpyHostToDevice, ctx->stream),
+               "tiles");
+  TSG_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream), "tiles");  // host arrays are stack-local
+  const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(L->desc.num_experts) * L->desc.d
+                                    : nullptr;
+  TSG_CUDA_TRY(ctx,
+               launch_gather_rows_gate(static_cast<const uint16_t*>(x), x_stride, rb.inv_rms,
+                                       rb.sorted_pairs, 0, static_cast<int>(T),
+                                       static_cast<int>(L->desc.d), 1, ctx->xp, gate_w,
+                                       rb.gate_raw, ctx->stream),
+               "gather");
+  CUtensorMap maps[2];
+  if (!encode_rows_map(&maps[0], ctx->xp, T, L->desc.d) ||
+      !encode_rows_map(&maps[1], ctx->act_buf, T, L->desc.f))
+    return fail(ctx, TSG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  QmmParams qp{};
+  qp.D = static_cast<int>(L->desc.d);
+  qp.F = static_cast<int>(L->desc.f);
+  qp.E = static_cast<int>(L->desc.num_experts);
+  qp.act = static_cast<int>(L->desc.activation);
+  qp.n_rows_total = static_cast<int>(T);
+  qp.experts = expert_set(L);
+  qp.row_tiles = rb.row_tiles;
+  qp.n_row_tiles = rb.n_row_tiles;
+  qp.xp = ctx->xp;
+  qp.act_buf = ctx->act_buf;
+  qp.partials = ctx->partials;
+  qp.err = rb.err;
+  qp.num_sms = ctx->num_sms;
+  qp.maps = maps;
+  TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, ctx->stream), "qmm gate/up");
+  TSG_CUDA_TRY(ctx, launch_qmm_down(qp, ctx->stream), "qmm down");
+  CombineParams cp{};
+  cp.T = static_cast<int>(T);
+  cp.D = static_cast<int>(L->desc.d);
+  cp.K = 0;
+  cp.has_shared = 1;
+  cp.partials = ctx->partials;
+  cp.pair_pos = rb.pair_pos;
+  cp.weights = rb.weights;
+  cp.gate_raw = L->has_gate ? rb.gate_raw : nullptr;
+  cp.inv_rms = rb.inv_rms;
+  cp.y = y;
+  cp.y_stride = y_stride;
+  cp.y_f32 = y_dtype == TSG_DTYPE_F32 ? 1 : 0;
+  TSG_CUDA_TRY(ctx, launch_combine(cp, ctx->stream), "combine");
+  return TSG_OK;
+}
+
+tsg_status tsg_last_routing(tsg_ctx ctx, const uint32_t** ids, const float** weights,
+                            const tsg_token_expert_pair** sorted_pairs, uint32_t* T, uint32_t* K) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  if (ids) *ids = ctx->rb.ids;
+  if (weights) *weights = ctx->rb.weights;
+  if (sorted_pairs) *sorted_pairs = reinterpret_cast<const tsg_token_expert_pair*>(ctx->rb.sorted_pairs);
+  if (T) *T = ctx->last_T;
+  if (K) *K = ctx->last_K;
+  return TSG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,164 @@
+// tsg_kernels.cuh -- launch-side declarations shared by the .cu files and the
+// C-ABI implementation.  Plain structs of device pointers and sizes.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tsg {
+
+// Byte offsets of an expert's sub-tensors inside its blob (MoEExpertOffsets,
+// Sources/Tsugumi/Kernels/MoE/MoE.swift:4-29).  Bias offsets are carried
+// for layout compatibility and never read: the scheme is symmetric.
+struct ExpertOffsets {
+  uint32_t gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b;
+};
+
+// 16-byte token/expert pair (PrefillTokenExpertPair,
+// Sources/Tsugumi/Kernels/Prefill/MoE/PrefillRouter.swift:4-28).
+struct Pair {
+  uint32_t token, expert, rank, weight_bits;
+};
+
+struct Group {
+  uint32_t expert, pair_start, pair_count;
+};
+
+struct Tile {
+  uint32_t group_start, group_count, pair_start, pair_count;
+};
+
+// One unit of the grouped contraction's schedule: `rows` consecutive sorted
+// rows starting at `row_start`, all routed to `expert` (expert == E marks
+// the shared expert).
+struct RowTile {
+  uint32_t expert, row_start, rows, pad;
+};
+
+// Everything a kernel needs to find an expert's weights.
+struct ExpertSet {
+  const uint8_t* base;     // expert 0's blob
+  uint64_t stride;         // bytes between blobs
+  ExpertOffsets off;
+  const uint8_t* shared;   // shared expert's blob, or nullptr
+  ExpertOffsets shared_off;
+};
+
+// Per-layer routing workspace written by the router / permutation kernels.
+struct RouteBuffers {
+  float* logits_raw;      // [ksplit, T, E] raw router dots (no norm factor)
+  float* gate_raw;        // [T] raw shared-gate dot w_s . x (no norm factor)
+  float* sumsq;           // [ksplit, T] row sums of squares
+  float* inv_rms;         // [T]
+  uint32_t* ids;          // [T, K]
+  float* weights;         // [T, K]
+  uint16_t* weights_f16;  // [T, K] (optional)
+  uint32_t* counts;       // [E]
+  uint32_t* offsets;      // [E] (0xFFFFFFFF when empty)
+  Pair* sorted_pairs;     // [T*K]
+  uint32_t* pair_pos;     // [T*K]: sorted position of token-major pair t*K+r
+  Group* groups;          // [E]
+  uint32_t* n_groups;     // [1]
+  Tile* tiles;            // [E]
+  uint32_t* n_tiles;      // [1]
+  RowTile* row_tiles;     // [ceil(T*K/tile_rows) + E + ceil(T/tile_rows)]
+  uint32_t* n_row_tiles;  // [1]
+  float* xn;              // [T, D] decode only: x * inv_rms in fp32
+  float* xs8;             // [T, D/8] decode only: 1.5 x sum of each 8-element run of xn
+  uint32_t* sync_counter; // [1] last-CTA counter, self-resetting
+  uint32_t* err;          // [1] device error word
+};
+
+struct RouterParams {
+  const uint16_t* x;       // [T, x_stride] bf16
+  uint32_t x_stride;
+  int T, D, E, K;
+  const float* w;          // [E + has_gate, D] router rows (effective scale folded in)
+  int has_gate;            // 1: row E is the shared-expert gate vector
+  int has_shared;          // 1: the layer has a shared expert
+  const float* per_expert_scale;  // [E] or nullptr
+  const float* logit_bias;        // [E] or nullptr
+  int norm;                // 1: no-scale RMSNorm of x
+  float eps;
+  int tile_rows;           // rows per RowTile in the schedule
+  int tile_expert_count;   // PrefillMoEGrouping tiles
+  int tile_break;          // forced tile cut after this group, -1 none
+  const uint64_t* sort_keys;  // [E] or nullptr
+};
+
+// router.cu
+cudaError_t launch_router_decode(const RouterParams& p, const RouteBuffers& rb,
+                                 cudaStream_t s);
+cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb,
+                                  cudaStream_t s);
+cudaError_t launch_rowprep(const RouterParams& p, const RouteBuffers& rb, int write_rows,
+                           cudaStream_t s);
+cudaError_t launch_group_small(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s);
+int router_prefill_ksplit(int T, int E, int D);
+// permute.cu
+cudaError_t launch_permute(const RouterParams& p, const RouteBuffers& rb, const Pair* pairs_in,
+                           cudaStream_t s);
+cudaError_t launch_make_pairs(const uint32_t* ids, const uint16_t* w_f16, int T, int K,
+                              Pair* out, cudaStream_t s);
+cudaError_t launch_gather_rows_gate(const uint16_t* x, uint32_t x_stride, const float* inv_rms,
+                                    const Pair* sorted_pairs, int n_rows, int T, int D,
+                                    int append_tokens, __half* xp, const float* gate_w,
+                                    float* gate_raw, cudaStream_t s);
+
+// decode.cu
+struct DecodeParams {
+  int T, D, F, E, K, act, has_shared;
+  const uint16_t* x;  // [T, x_stride] bf16
+  uint32_t x_stride;
+  ExpertSet experts;
+  RouteBuffers rb;
+  __half* act_buf;    // [T*K + T, F]
+  const float* xn;    // [T, D] normalised input, fp32 (written by the router)
+  const float* xs8;   // [T, D/8] 1.5 x sums of 8-element runs of xn
+  void* y;            // [T, y_stride]
+  uint32_t y_stride;
+  int y_f32;
+  const float* residual;  // [T, D] fp32 or nullptr
+  int num_sms;
+};
+cudaError_t launch_decode_experts(const DecodeParams& p, cudaStream_t s);
+cudaError_t launch_decode_gate_up(const DecodeParams& p, cudaStream_t s);
+cudaError_t launch_decode_down(const DecodeParams& p, cudaStream_t s);
+
+// umma.cu
+struct QmmParams {
+  int D, F, E, act, n_rows_total;  // n_rows_total: rows of xp / act / partials
+  ExpertSet experts;
+  const RowTile* row_tiles;
+  const uint32_t* n_row_tiles;
+  int max_row_tiles;
+  const __half* xp;      // [rows, D] fp16 (GEMM1 input)
+  __half* act_buf;       // [rows, F] fp16 (GEMM1 output, GEMM2 input)
+  __half* partials;      // [rows, D] fp16 (GEMM2 output)
+  uint32_t* err;
+  int num_sms;
+  const CUtensorMap* maps;  // host copies: [0] xp rows, [1] act rows
+};
+cudaError_t launch_qmm_gate_up(const QmmParams& p, cudaStream_t s);
+cudaError_t launch_qmm_down(const QmmParams& p, cudaStream_t s);
+int qmm_tile_rows();
+
+// combine.cu
+struct CombineParams {
+  int T, D, K, has_shared, E;
+  const __half* partials;   // [T*K (+T), D] in sorted order (+ shared rows in token order)
+  const uint32_t* pair_pos; // [T*K]
+  const float* weights;     // [T, K]
+  const float* gate_raw;    // [T] raw shared-gate dot, or nullptr (ungated)
+  const float* inv_rms;     // [T]
+  const float* residual;    // [T, D] fp32 or nullptr
+  void* y;
+  uint32_t y_stride;
+  int y_f32;
+};
+cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
+cudaError_t launch_reduce_token_major(const __half* partials, const float* w, int T, int K, int D,
+                                      void* h2, int h2_f32, cudaStream_t s);
+
+}  // namespace tsg
