@@ -123,8 +123,16 @@ TSG_API int tsg_abi_version(void);
 TSG_API tsg_status tsg_ctx_create(int device, void *stream, tsg_ctx *out);
 TSG_API tsg_status tsg_ctx_destroy(tsg_ctx ctx);
 TSG_API tsg_status tsg_ctx_set_stream(tsg_ctx ctx, void *stream);
-/* Largest T handled by the decode (batched GEMV) regime; default 64. */
+/* Largest T handled by the decode regime; default 4 (the single fused
+ * kernel).  Larger T goes to the grouped tcgen05 contraction. */
 TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
+/* Tuning switches: "fused_decode" (1: T <= 4 runs the whole block as one
+ * cooperative kernel, default; 0: router / gate-up / down kernels) and
+ * "programmatic_launch" (1: allow the next kernel on the stream to launch
+ * while this one finishes) and "debug_phase_stamps" (a device address of
+ * num_sms x 8 uint64 the fused decode kernel fills with %globaltimer stamps
+ * at its phase boundaries, or 0 for none). */
+TSG_API tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char *name, int64_t value);
 /* Pre-allocates the workspace for up to max_tokens tokens of this layer's
  * shape, so later calls allocate nothing (required before stream capture). */
 TSG_API tsg_status tsg_ctx_reserve(tsg_ctx ctx, tsg_moe_layer layer, uint32_t max_tokens);
@@ -133,7 +141,10 @@ TSG_API tsg_status tsg_ctx_reserve(tsg_ctx ctx, tsg_moe_layer layer, uint32_t ma
 TSG_API tsg_status tsg_sync(tsg_ctx ctx);
 TSG_API const char *tsg_last_error_string(tsg_ctx ctx);
 
-/* ---- layers ---- */
+/* ---- layers ----
+ * A layer must be destroyed before its context is used with another device;
+ * destroying the context first is allowed (the layer then only frees its own
+ * router copy). */
 TSG_API tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc *desc, tsg_moe_layer *out);
 TSG_API tsg_status tsg_moe_layer_destroy(tsg_moe_layer layer);
 

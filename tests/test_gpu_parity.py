@@ -30,14 +30,15 @@ def rel_l2(a, b) -> float:
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
+_LAYERS: dict = {}
+
+
 @pytest.fixture(scope="module")
 def ctx():
     c = tb.Context(0)
     yield c
+    _LAYERS.clear()
     c.close()
-
-
-_LAYERS: dict = {}
 
 
 def layer_pair(ctx, name, seed, skew=None):
@@ -47,6 +48,22 @@ def layer_pair(ctx, name, seed, skew=None):
         dev = tb.MoELayer(ctx, tb.upload_host_layer(host))
         _LAYERS[key] = (host, dev, O.OracleLayer(host))
     return _LAYERS[key]
+
+
+class regime:
+    """Temporarily selects the regime: decode_max_tokens and the fused
+    single-kernel decode switch."""
+
+    def __init__(self, ctx, dmax=4, fused=True):
+        self.ctx, self.dmax, self.fused = ctx, dmax, fused
+
+    def __enter__(self):
+        self.ctx.set_decode_max_tokens(self.dmax)
+        self.ctx.set_option("fused_decode", 1 if self.fused else 0)
+
+    def __exit__(self, *exc):
+        self.ctx.set_decode_max_tokens(4)
+        self.ctx.set_option("fused_decode", 1)
 
 
 def gpu_route(ctx, layer, x_dev):
@@ -78,12 +95,9 @@ ROUTER_CASES = [
 @pytest.mark.parametrize("name,T,skew,dmax", ROUTER_CASES)
 def test_router_topk_matches_oracle(ctx, name, T, skew, dmax):
     host, dev, ol = layer_pair(ctx, name, 11, skew)
-    ctx.set_decode_max_tokens(dmax)
-    try:
-        x = host_tokens(T, host.d, 100 + T)
+    x = host_tokens(T, host.d, 100 + T)
+    with regime(ctx, dmax):
         ids, w, w16 = gpu_route(ctx, dev, to_dev(x))
-    finally:
-        ctx.set_decode_max_tokens(64)
     ref_ids, ref_w, gap, _ = ol.router(x)
     ok = gap >= TIE_GAP
     assert ok.sum() >= T - 1
@@ -170,62 +184,93 @@ def test_grouping_rejects_bad_arguments(ctx):
 
 
 BLOCK_CASES = [
-    # name, T, skew, decode_max_tokens, oracle token sample
-    ("tiny", 16, None, 64, None),
-    ("gemma", 1, None, 64, None),
-    ("gemma", 4, None, 64, None),
-    ("gemma", 16, None, 64, None),
-    ("gemma", 64, None, 64, None),
-    ("qwen", 1, None, 64, None),
-    ("qwen", 64, None, 64, None),
-    ("tiny", 200, None, 64, None),
-    ("gemma", 512, None, 64, 48),
-    ("gemma", 4096, 1.1, 64, 48),
-    ("qwen", 1024, None, 64, 48),
-    ("gemma", 48, None, 0, None),  # prefill kernels at a decode size
+    # name, T, skew, decode_max_tokens, fused, oracle token sample
+    ("tiny", 4, None, 4, True, None),
+    ("gemma", 1, None, 4, True, None),
+    ("gemma", 2, None, 4, True, None),
+    ("gemma", 4, None, 4, True, None),
+    ("qwen", 1, None, 4, True, None),
+    ("qwen", 4, None, 4, True, None),
+    ("tiny", 16, None, 64, False, None),
+    ("gemma", 1, None, 64, False, None),
+    ("gemma", 16, None, 64, False, None),
+    ("gemma", 64, None, 64, False, None),
+    ("qwen", 64, None, 64, False, None),
+    ("gemma", 16, None, 4, True, None),   # T > 4: grouped tcgen05 path
+    ("tiny", 200, None, 4, True, None),
+    ("gemma", 512, None, 4, True, 48),
+    ("gemma", 4096, 1.1, 4, True, 48),
+    ("qwen", 1024, None, 4, True, 48),
+    ("gemma", 48, None, 0, True, None),
 ]
 
 
-@pytest.mark.parametrize("name,T,skew,dmax,sample", BLOCK_CASES)
-def test_block_forward_matches_oracle(ctx, name, T, skew, dmax, sample):
+@pytest.mark.parametrize("name,T,skew,dmax,fused,sample", BLOCK_CASES)
+def test_block_forward_matches_oracle(ctx, name, T, skew, dmax, fused, sample):
     host, dev, ol = layer_pair(ctx, name, 11, skew)
     x = host_tokens(T, host.d, 7 + T)
     xd = to_dev(x)
-    ctx.set_decode_max_tokens(dmax)
-    try:
-        ids, w, _ = gpu_route(ctx, dev, xd)
+    with regime(ctx, dmax, fused):
         y = dev.forward(xd, out_dtype=torch.float32)
         ctx.sync()
-    finally:
-        ctx.set_decode_max_tokens(64)
+    ids, w, _ = gpu_route(ctx, dev, xd)
+    ref_ids, _, gap, _ = ol.router(x)
+    ok = gap >= TIE_GAP
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32)[ok], ref_ids[ok])
     rows = np.arange(T) if sample is None else np.linspace(0, T - 1, sample).astype(int)
     y_ref, _, _ = ol.block(x[rows], ids.cpu().numpy()[rows].astype(np.uint32),
                            w.cpu().numpy()[rows])
     y_gpu = y.cpu().numpy()[rows]
     err = rel_l2(y_gpu, y_ref)
-    print(f"{name} T={T}: rel L2 {err:.3e}")
+    print(f"{name} T={T} fused={fused} dmax={dmax}: rel L2 {err:.3e}")
     assert np.all(np.isfinite(y_gpu))
     assert err <= REL_L2
 
 
-@pytest.mark.parametrize("name,T", [("gemma", 8), ("qwen", 32)])
+@pytest.mark.parametrize("name,T", [("gemma", 1), ("qwen", 3)])
+def test_fused_decode_graph_replay_is_stable(ctx, name, T):
+    """Replaying the fused kernel from a CUDA graph (its grid counters reset
+    themselves at the end of every launch) gives the same bits every time,
+    equal to a plain launch."""
+    host, dev, ol = layer_pair(ctx, name, 11, None)
+    xd = to_dev(host_tokens(T, host.d, 77))
+    y0 = dev.forward(xd, out_dtype=torch.float32)
+    ctx.sync()
+    ctx.reserve(dev, T)
+    y = torch.empty((T, host.d), dtype=torch.float32, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        ctx.set_stream(side)
+        with torch.cuda.graph(g, stream=side):
+            dev.forward(xd, y=y)
+    torch.cuda.current_stream().wait_stream(side)
+    ctx.set_stream(torch.cuda.current_stream())
+    for _ in range(5):
+        y.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y, y0)
+    ctx.sync()
+    del g
+
+
+@pytest.mark.parametrize("name,T", [("gemma", 4), ("qwen", 32)])
 def test_decode_and_prefill_regimes_agree(ctx, name, T):
     host, dev, ol = layer_pair(ctx, name, 11, None)
     xd = to_dev(host_tokens(T, host.d, 3))
-    y_dec = dev.forward(xd, out_dtype=torch.float32)
-    ctx.set_decode_max_tokens(0)
-    try:
+    with regime(ctx, 64, False):
+        y_dec = dev.forward(xd, out_dtype=torch.float32)
+    with regime(ctx, 0):
         y_pre = dev.forward(xd, out_dtype=torch.float32)
         ctx.sync()
-    finally:
-        ctx.set_decode_max_tokens(64)
     assert rel_l2(y_pre.cpu().numpy(), y_dec.cpu().numpy()) < REL_L2
 
 
-@pytest.mark.parametrize("regime", ["decode", "prefill"])
-def test_experts_with_caller_routing(ctx, regime):
+@pytest.mark.parametrize("which,T", [("decode", 3), ("decode", 8), ("prefill", 200)])
+def test_experts_with_caller_routing(ctx, which, T):
     host, dev, ol = layer_pair(ctx, "gemma", 11, None)
-    T = 8 if regime == "decode" else 200
     x = host_tokens(T, host.d, 55)
     rng = np.random.default_rng(5)
     ids = np.stack([rng.choice(host.num_experts, host.top_k, replace=False) for _ in range(T)])
@@ -235,7 +280,7 @@ def test_experts_with_caller_routing(ctx, regime):
     idt = torch.from_numpy(ids.astype(np.int32)).cuda()
     wt = torch.from_numpy(w).cuda()
     rt = torch.from_numpy(resid).cuda()
-    if regime == "decode":
+    if which == "decode":
         tb.MoE(ctx, dev).encode_routed_phases(to_dev(x), idt, wt, y, residual=rt)
     else:
         tb.PrefillGroupedRoutedMoE(ctx, dev).encode_streamed_tiled(to_dev(x), idt, wt, y,

@@ -76,6 +76,7 @@ SIGNATURES = [
     ("tsg_ctx_destroy", _S, [_P]),
     ("tsg_ctx_set_stream", _S, [_P, _P]),
     ("tsg_ctx_set_decode_max_tokens", _S, [_P, _U]),
+    ("tsg_ctx_set_option", _S, [_P, C.c_char_p, C.c_int64]),
     ("tsg_ctx_reserve", _S, [_P, _P, _U]),
     ("tsg_sync", _S, [_P]),
     ("tsg_last_error_string", C.c_char_p, [_P]),

@@ -50,7 +50,7 @@ struct tsg_ctx_s {
   int device = 0;
   cudaStream_t stream = nullptr;
   int num_sms = 148;
-  uint32_t decode_max_tokens = 64;
+  uint32_t decode_max_tokens = 4;
   std::string last_error;
   // workspace
   void* ws = nullptr;
@@ -60,6 +60,17 @@ struct tsg_ctx_s {
   __half* act_buf = nullptr;
   __half* xp = nullptr;
   __half* partials = nullptr;
+  // fused decode scratch
+  float* f_logits = nullptr;
+  void* f_xfrag = nullptr;
+  float* f_xsum = nullptr;
+  void* f_actfrag = nullptr;
+  float* f_actsum = nullptr;
+  float* f_vpart = nullptr;
+  uint32_t* f_counters = nullptr;
+  bool use_fused = true;
+  bool allow_pdl = false;
+  unsigned long long* stamps = nullptr;  // debug phase timestamps (device)
   // device status words: [0] error bits, [1] code, [2] value, [3] pad;
   // [4] last-CTA counter
   uint32_t* status = nullptr;
@@ -107,7 +118,8 @@ tsg_status fail(tsg_ctx ctx, tsg_status st, const std::string& msg) {
 
 tsg_status cuda_fail(tsg_ctx ctx, cudaError_t e, const char* where) {
   return fail(ctx, e == cudaErrorMemoryAllocation ? TSG_ERR_OOM : TSG_ERR_CUDA,
-              std::string(where) + ": " + cudaGetErrorString(e));
+              std::string(where) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) +
+                  ")");
 }
 
 #define TSG_CUDA_TRY(ctx, expr, where)                 \
@@ -163,7 +175,24 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
   __half* act = static_cast<__half*>(take(rows * F * 2));
   __half* xp = static_cast<__half*>(take(rows * D * 2));
   __half* part = static_cast<__half*>(take(rows * D * 2));
+  // fused decode (T <= 4)
+  const size_t Tf = std::min<size_t>(T, 4);
+  const size_t rows_f = Tf * K + Tf;
+  float* f_logits = static_cast<float*>(take(Tf * (E + 1) * 4));
+  void* f_xfrag = take(Tf * D * 2);
+  float* f_xsum = static_cast<float*>(take(Tf * (D / 32) * 4));
+  void* f_actfrag = take(rows_f * F * 2);
+  float* f_actsum = static_cast<float*>(take(rows_f * (F / 8) * 4));
+  float* f_vpart = static_cast<float*>(take(rows_f * D * 4));
+  uint32_t* f_counters = static_cast<uint32_t*>(take((4 + D / 16) * 4));
   if (base) {
+    ctx->f_logits = f_logits;
+    ctx->f_xfrag = f_xfrag;
+    ctx->f_xsum = f_xsum;
+    ctx->f_actfrag = f_actfrag;
+    ctx->f_actsum = f_actsum;
+    ctx->f_vpart = f_vpart;
+    ctx->f_counters = f_counters;
     rb.sync_counter = ctx->status + 4;
     rb.err = ctx->status;
     ctx->rb = rb;
@@ -190,6 +219,9 @@ tsg_status ensure_workspace(tsg_ctx ctx, const Caps& want) {
   ctx->ws_bytes = bytes;
   ctx->caps = c;
   carve(ctx, c, static_cast<uint8_t*>(p));
+  // the fused decode kernel's counters must start at zero (they reset
+  // themselves at the end of every launch)
+  TSG_CUDA_TRY(ctx, cudaMemset(ctx->f_counters, 0, (4 + c.D / 16) * 4), "cudaMemset");
   return TSG_OK;
 }
 
@@ -248,10 +280,34 @@ bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Records stage boundary `k` (0..4) of the current profiled call.
+// Records stage boundary `k` (0..4) of the current profiled call.  Inside
+// stream capture the record must be "external" to become a graph node that
+// every replay re-records (a plain record there only orders streams);
+// outside capture a plain record is used.  Profiling never leaves an error
+// behind: on failure it switches itself off.
 void prof_mark(tsg_ctx ctx, int k) {
   if (!ctx->profiling || ctx->prof_calls >= ctx->prof_max) return;
-  cudaEventRecord(ctx->prof_events[ctx->prof_calls * 5 + k], ctx->stream);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(ctx->stream, &cs);
+  cudaEvent_t ev = ctx->prof_events[ctx->prof_calls * 5 + k];
+  if (e == cudaSuccess) {
+    e = cs == cudaStreamCaptureStatusActive
+            ? cudaEventRecordWithFlags(ev, ctx->stream, cudaEventRecordExternal)
+            : cudaEventRecord(ev, ctx->stream);
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    ctx->profiling = false;
+  }
+}
+
+// A CUDA error left pending by earlier work (ours or the caller's) would be
+// misattributed to the next launch; report it at the entry instead.
+tsg_status take_pending_error(tsg_ctx ctx) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return TSG_OK;
+  return fail(ctx, TSG_ERR_CUDA, std::string("error pending from earlier CUDA work: ") +
+                                     cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
 }
 
 bool valid_dtype(tsg_dtype t) { return t == TSG_DTYPE_BF16 || t == TSG_DTYPE_F32; }
@@ -288,6 +344,63 @@ tsg_status run_decode_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, ui
   prof_mark(ctx, 3);
   prof_mark(ctx, 4);
   return TSG_OK;
+}
+
+tsg_status run_decode_fused(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
+                            uint32_t T, const uint32_t* ids_in, const float* w_in,
+                            const float* residual, void* y, uint32_t y_stride, tsg_dtype y_dtype,
+                            uint32_t* ids_out, float* w_out, uint16_t* w16_out) {
+  DecodeFusedArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.x_stride = x_stride;
+  a.T = static_cast<int>(T);
+  a.D = static_cast<int>(L->desc.d);
+  a.F = static_cast<int>(L->desc.f);
+  a.E = static_cast<int>(L->desc.num_experts);
+  a.K = static_cast<int>(L->desc.top_k);
+  a.act = static_cast<int>(L->desc.activation);
+  a.norm = L->desc.router_norm ? 1 : 0;
+  a.eps = L->desc.norm_eps;
+  a.router_rows = L->router_rows;
+  a.has_gate = L->has_gate;
+  a.has_shared = L->has_shared;
+  a.per_expert_scale = L->desc.per_expert_scale;
+  a.logit_bias = L->desc.logit_bias;
+  a.ids_in = ids_in;
+  a.w_in = w_in;
+  a.experts = expert_set(L);
+  a.y = y;
+  a.y_stride = y_stride;
+  a.y_f32 = y_dtype == TSG_DTYPE_F32 ? 1 : 0;
+  a.residual = residual;
+  a.logits = ctx->f_logits;
+  a.inv_rms = ctx->rb.inv_rms;
+  a.xfrag = ctx->f_xfrag;
+  a.xsum = ctx->f_xsum;
+  a.actfrag = ctx->f_actfrag;
+  a.actsum = ctx->f_actsum;
+  a.vpart = ctx->f_vpart;
+  a.counters = ctx->f_counters;
+  a.ids_out = ids_out;
+  a.w_out = w_out;
+  a.w16_out = w16_out;
+  a.pairs_out = ctx->rb.sorted_pairs;
+  a.err = ctx->rb.err;
+  a.num_sms = ctx->num_sms;
+  a.allow_pdl = ctx->allow_pdl ? 1 : 0;
+  a.stamps = ctx->stamps;
+  TSG_CUDA_TRY(ctx, launch_decode_fused(a, ctx->stream), "fused decode");
+  prof_mark(ctx, 1);
+  prof_mark(ctx, 2);
+  prof_mark(ctx, 3);
+  prof_mark(ctx, 4);
+  return TSG_OK;
+}
+
+bool fused_ok(tsg_ctx ctx, const tsg_moe_layer_s* L, uint32_t T) {
+  return ctx->use_fused &&
+         decode_fused_supported(static_cast<int>(T), static_cast<int>(L->desc.top_k),
+                                static_cast<int>(L->desc.num_experts), L->has_gate, ctx->num_sms);
 }
 
 tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
@@ -447,6 +560,17 @@ tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t) {
   return TSG_OK;
 }
 
+tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char* name, int64_t value) {
+  if (!ctx || !name) return fail(ctx, TSG_ERR_INVALID_ARG, "null argument");
+  const std::string n(name);
+  if (n == "fused_decode") ctx->use_fused = value != 0;
+  else if (n == "programmatic_launch") ctx->allow_pdl = value != 0;
+  else if (n == "debug_phase_stamps")
+    ctx->stamps = reinterpret_cast<unsigned long long*>(static_cast<uintptr_t>(value));
+  else return fail(ctx, TSG_ERR_INVALID_ARG, "unknown option " + n);
+  return TSG_OK;
+}
+
 tsg_status tsg_ctx_reserve(tsg_ctx ctx, tsg_moe_layer layer, uint32_t max_tokens) {
   if (!ctx || !layer) return fail(ctx, TSG_ERR_INVALID_ARG, "null context or layer");
   return ensure_workspace(ctx, layer_caps(layer, max_tokens));
@@ -527,7 +651,8 @@ tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc* d, tsg_mo
 
 tsg_status tsg_moe_layer_destroy(tsg_moe_layer L) {
   if (!L) return TSG_ERR_INVALID_ARG;
-  if (L->ctx) cudaStreamSynchronize(L->ctx->stream);
+  // the layer does not touch its context here: contexts and layers may be
+  // destroyed in either order (cudaFree waits for outstanding work itself)
   if (L->router_rows) cudaFree(L->router_rows);
   delete L;
   return TSG_OK;
@@ -705,6 +830,8 @@ tsg_status tsg_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidde
                                  void* y, uint32_t y_stride, tsg_dtype y_dtype) {
   tsg_status st = check_common(ctx, L, hidden, hidden_stride, T, y, y_stride, y_dtype);
   if (st != TSG_OK || T == 0) return st;
+  st = take_pending_error(ctx);
+  if (st != TSG_OK) return st;
   st = ensure_workspace(ctx, layer_caps(L, T));
   if (st != TSG_OK) return st;
   RouterParams p = router_params(L, hidden, hidden_stride, T);
@@ -712,7 +839,10 @@ tsg_status tsg_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidde
   ctx->last_K = L->desc.top_k;
   prof_mark(ctx, 0);
   tsg_status r;
-  if (T <= ctx->decode_max_tokens) {
+  if (T <= ctx->decode_max_tokens && fused_ok(ctx, L, T)) {
+    r = run_decode_fused(ctx, L, hidden, hidden_stride, T, nullptr, nullptr, residual, y, y_stride,
+                         y_dtype, ctx->rb.ids, ctx->rb.weights, ctx->rb.weights_f16);
+  } else if (T <= ctx->decode_max_tokens) {
     TSG_CUDA_TRY(ctx, launch_router_decode(p, ctx->rb, ctx->stream), "router (decode)");
     prof_mark(ctx, 1);
     r = run_decode_experts(ctx, L, hidden, hidden_stride, T, residual, y, y_stride, y_dtype);
@@ -773,6 +903,10 @@ static tsg_status experts_with_routing(tsg_ctx ctx, tsg_moe_layer L, const void*
   RouterParams p = router_params(L, x, x_stride, T);
   ctx->last_T = T;
   ctx->last_K = L->desc.top_k;
+  if (decode && fused_ok(ctx, L, T)) {
+    return run_decode_fused(ctx, L, x, x_stride, T, ctx->rb.ids, ctx->rb.weights, residual, y,
+                            y_stride, y_dtype, nullptr, nullptr, nullptr);
+  }
   TSG_CUDA_TRY(ctx, launch_rowprep(p, ctx->rb, decode ? 1 : 0, ctx->stream), "row prep");
   if (decode) {
     TSG_CUDA_TRY(ctx, launch_group_small(p, ctx->rb, ctx->stream), "group");

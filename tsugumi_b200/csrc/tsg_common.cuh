@@ -34,8 +34,16 @@ inline cudaError_t allow_max_smem_ptr(const void* k) {
   static std::unordered_set<const void*> done;
   std::lock_guard<std::mutex> lock(mu);
   if (done.count(k)) return cudaSuccess;
-  const cudaError_t e =
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  // the opt-in limit covers static + dynamic shared memory together
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess)
+    e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes fa;
+  if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, k);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - static_cast<int>(fa.sharedSizeBytes));
   if (e == cudaSuccess) done.insert(k);
   return e;
 }

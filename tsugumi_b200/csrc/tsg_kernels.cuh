@@ -126,6 +126,44 @@ cudaError_t launch_decode_experts(const DecodeParams& p, cudaStream_t s);
 cudaError_t launch_decode_gate_up(const DecodeParams& p, cudaStream_t s);
 cudaError_t launch_decode_down(const DecodeParams& p, cudaStream_t s);
 
+// decode_fused.cu: the whole block for T <= 4 in one cooperative kernel
+struct DecodeFusedArgs {
+  const uint16_t* x;
+  uint32_t x_stride;
+  int T, D, F, E, K, act, norm;
+  float eps;
+  const float* router_rows;
+  int has_gate, has_shared;
+  const float* per_expert_scale;
+  const float* logit_bias;
+  const uint32_t* ids_in;  // caller routing, or nullptr
+  const float* w_in;
+  ExpertSet experts;
+  void* y;
+  uint32_t y_stride;
+  int y_f32;
+  const float* residual;
+  float* logits;    // [T][E + 1]
+  float* inv_rms;   // [T]
+  void* xfrag;      // [T][D] fp16, fragment order
+  float* xsum;      // [T][D / 32]
+  void* actfrag;    // [T*K + T][F] fp16, fragment order
+  float* actsum;    // [T*K + T][F / 8]
+  float* vpart;     // [T*K + T][D]
+  uint32_t* counters;  // [4 + D / 16], zero between launches
+  uint32_t* ids_out;
+  float* w_out;
+  uint16_t* w16_out;
+  Pair* pairs_out;
+  uint32_t* err;
+  int num_sms;
+  int allow_pdl;
+  unsigned long long* stamps;  // debug phase timestamps [grid][8], or nullptr
+};
+bool decode_fused_supported(int T, int K, int E, int has_gate, int num_sms);
+size_t decode_fused_smem(int T, int D, int F, int K, int E, int has_gate, int num_sms);
+cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t s);
+
 // umma.cu
 struct QmmParams {
   int D, F, E, act, n_rows_total;  // n_rows_total: rows of xp / act / partials

@@ -11,6 +11,7 @@ Errors surface as exceptions named like the reference's thrown errors.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 from dataclasses import dataclass
 
 import numpy as np
@@ -48,12 +49,16 @@ class Context:
         s = None if stream is None else C.c_void_p(stream.cuda_stream)
         check(self.lib.tsg_ctx_create(device, s, C.byref(h)))
         self.h = h
+        self._layers = weakref.WeakSet()
 
     def set_stream(self, stream) -> None:
         check(self.lib.tsg_ctx_set_stream(self.h, C.c_void_p(stream.cuda_stream)), self.h)
 
     def set_decode_max_tokens(self, t: int) -> None:
         check(self.lib.tsg_ctx_set_decode_max_tokens(self.h, t), self.h)
+
+    def set_option(self, name: str, value: int) -> None:
+        check(self.lib.tsg_ctx_set_option(self.h, name.encode(), int(value)), self.h)
 
     def reserve(self, layer: "MoELayer", max_tokens: int) -> None:
         check(self.lib.tsg_ctx_reserve(self.h, layer.h, max_tokens), self.h)
@@ -71,6 +76,8 @@ class Context:
 
     def close(self) -> None:
         if self.h:
+            for layer in list(self._layers):
+                layer.close()
             self.lib.tsg_ctx_destroy(self.h)
             self.h = None
 
@@ -115,6 +122,7 @@ class MoELayer:
         h = C.c_void_p()
         check(ctx.lib.tsg_moe_layer_create(ctx.h, C.byref(d), C.byref(h)), ctx.h)
         self.h = h
+        ctx._layers.add(self)
         self.d, self.f = t["d"], t["f"]
         self.num_experts, self.top_k = t["num_experts"], t["top_k"]
 
