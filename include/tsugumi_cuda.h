@@ -189,6 +189,37 @@ TSG_API tsg_status tsg_moe_group_pairs(tsg_ctx ctx, const tsg_token_expert_pair 
                                uint32_t *per_expert_counts, tsg_moe_group *groups,
                                uint32_t *n_groups, tsg_moe_tile *tiles, uint32_t *n_tiles);
 
+/* No counterpart in the reference.  Same arguments, checks and outputs as
+ * tsg_moe_group_pairs, but the call allocates no device memory: the
+ * permutation's scratch (token-major ids and fp16 weights, the per-slot
+ * occupancy flags and sorted positions, the row-tile schedule, and one
+ * CTA-completion counter) lives in one fixed static device array of
+ * TSG_GROUP_NOALLOC_SCRATCH_BYTES inside this library, instead of the
+ * context's workspace, which tsg_moe_group_pairs may grow with cudaMalloc.
+ * It is for hosts that must not allocate from inside their enqueue path:
+ * a runtime that has reserved its device memory up front, or one for which
+ * the device-wide synchronisation of cudaFree would stall other streams.
+ * Limits: n_pairs <= TSG_GROUP_NOALLOC_MAX_PAIRS and num_experts <= 512;
+ * larger calls return TSG_ERR_UNSUPPORTED_SHAPE with a message naming the
+ * limit, before any work is enqueued.
+ * - The first call on each device resolves the array's address for that
+ *   device (cudaGetSymbolAddress, with the context's device current); make
+ *   that first call before recording the context's stream into anything.
+ * - The completion counter must be zero when a call starts.  It is zero
+ *   when the library loads and each call leaves it at zero.
+ * - The array is shared by every caller on a device: two calls whose work
+ *   can overlap on the GPU (different streams, or different contexts of the
+ *   same device, without an ordering between them) race on it and corrupt
+ *   each other's results.  Order such calls, or use tsg_moe_group_pairs. */
+#define TSG_GROUP_NOALLOC_MAX_PAIRS 65536u
+#define TSG_GROUP_NOALLOC_SCRATCH_BYTES (1u << 20)
+TSG_API tsg_status tsg_moe_group_pairs_noalloc(
+    tsg_ctx ctx, const tsg_token_expert_pair *pairs, uint32_t n_pairs, int32_t query_count,
+    int32_t top_k, int32_t num_experts, int32_t tile_expert_count, const uint64_t *sort_keys,
+    int32_t n_sort_keys, int32_t tile_break_after_group, tsg_token_expert_pair *sorted_pairs,
+    uint32_t *per_expert_offsets, uint32_t *per_expert_counts, tsg_moe_group *groups,
+    uint32_t *n_groups, tsg_moe_tile *tiles, uint32_t *n_tiles);
+
 /* PrefillRoutedGEMMPlanner.plan (PrefillGroupedRoutedMoE.swift:42-83), host
  * function on host arrays.  Writes up to max_blocks blocks and up to
  * max_batches batches (rows, first block, block count); returns

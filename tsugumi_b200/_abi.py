@@ -87,6 +87,8 @@ SIGNATURES = [
     ("tsg_make_token_expert_pairs", _S, [_P, _P, _P, _U, _U, _P]),
     ("tsg_moe_group_pairs", _S, [_P, _P, _U, _I, _I, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P,
                                  _P, _P]),
+    ("tsg_moe_group_pairs_noalloc", _S, [_P, _P, _U, _I, _I, _I, _I, _P, _I, _I, _P, _P, _P,
+                                         _P, _P, _P, _P]),
     ("tsg_plan_routed_gemm", _S, [_P, _U, _U, _U, _P, _U, C.POINTER(_U), _P, _P, _P, _U,
                                   C.POINTER(_U)]),
     ("tsg_moe_experts_decode", _S, [_P, _P, _P, _U, _U, _P, _P, _P, _P, _U, C.c_int]),

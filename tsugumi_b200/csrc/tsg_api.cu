@@ -507,6 +507,60 @@ __global__ void fold_router_kernel(const float* w, const float* eff, const float
 
 }  // namespace
 
+// ---- scratch of tsg_moe_group_pairs_noalloc --------------------------------
+// Some hosts cannot let a library allocate device memory once they are
+// running: a serving runtime that carved all of HBM into its own pools at
+// start-up sees a cudaMalloc fail or eat into memory it promised elsewhere,
+// and cudaFree waits for the whole device, stalling every other stream the
+// host keeps busy.  tsg_moe_group_pairs may grow the context workspace with
+// both, so the no-alloc variant takes its scratch from this one array,
+// sized for TSG_GROUP_NOALLOC_MAX_PAIRS pairs and 512 experts.  Device
+// globals are zero when the module loads; the one word that must be zero
+// at the start of a call (the count kernel's CTA-completion counter) is
+// reset by the last CTA of every call.
+static __device__ __align__(256) uint8_t g_group_scratch[TSG_GROUP_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr size_t kGsPairs = TSG_GROUP_NOALLOC_MAX_PAIRS;
+constexpr uint32_t kGsExperts = 512;
+// Row tiles for any tile height >= 16 (max_row_tiles with T <= P).
+constexpr size_t kGsRowTiles = 2 * (kGsPairs / 16 + 1) + kGsExperts + 1;
+constexpr size_t gs_align(size_t x) { return (x + 255) / 256 * 256; }
+constexpr size_t kGsOffIds = 0;                                         // u32 [P]
+constexpr size_t kGsOffW16 = kGsOffIds + gs_align(kGsPairs * 4);        // u16 [P]
+constexpr size_t kGsOffPos = kGsOffW16 + gs_align(kGsPairs * 2);        // u32 [P]
+constexpr size_t kGsOffTiles = kGsOffPos + gs_align(kGsPairs * 4);      // RowTile [..]
+constexpr size_t kGsOffNTiles = kGsOffTiles + gs_align(kGsRowTiles * sizeof(RowTile));
+constexpr size_t kGsOffCounter = kGsOffNTiles + 256;                    // u32, zero between calls
+constexpr size_t kGsEnd = kGsOffCounter + 256;
+static_assert(kGsEnd <= TSG_GROUP_NOALLOC_SCRATCH_BYTES, "group scratch layout overflows");
+
+constexpr int kGsMaxDevices = 64;
+std::mutex g_gs_mu;
+uint8_t* g_gs_addr[kGsMaxDevices] = {};
+
+// The array's address on ctx's device, resolved on the first call for that
+// device with the device current and kept for the life of the process.
+tsg_status group_scratch_on(tsg_ctx ctx, uint8_t** out) {
+  if (ctx->device < 0 || ctx->device >= kGsMaxDevices)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_gs_mu);
+  if (!g_gs_addr[ctx->device]) {
+    TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    void* p = nullptr;
+    TSG_CUDA_TRY(ctx, cudaGetSymbolAddress(&p, g_group_scratch),
+                 "cudaGetSymbolAddress(group scratch)");
+    if (!p || reinterpret_cast<uintptr_t>(p) % 256 != 0)
+      return fail(ctx, TSG_ERR_CUDA, "group scratch: unexpected symbol address");
+    g_gs_addr[ctx->device] = static_cast<uint8_t*>(p);
+  }
+  *out = g_gs_addr[ctx->device];
+  return TSG_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int tsg_abi_version(void) { return TSG_ABI_VERSION; }
@@ -767,6 +821,107 @@ tsg_status tsg_moe_group_pairs(tsg_ctx ctx, const tsg_token_expert_pair* pairs, 
   }
   TSG_CUDA_TRY(ctx, launch_permute(p, rb, reinterpret_cast<const Pair*>(pairs), ctx->stream),
                "group pairs");
+  return TSG_OK;
+}
+
+tsg_status tsg_moe_group_pairs_noalloc(tsg_ctx ctx, const tsg_token_expert_pair* pairs,
+                                       uint32_t n_pairs, int32_t query_count, int32_t top_k,
+                                       int32_t num_experts, int32_t tile_expert_count,
+                                       const uint64_t* sort_keys, int32_t n_sort_keys,
+                                       int32_t tile_break, tsg_token_expert_pair* sorted_pairs,
+                                       uint32_t* offsets, uint32_t* counts, tsg_moe_group* groups,
+                                       uint32_t* n_groups, tsg_moe_tile* tiles,
+                                       uint32_t* n_tiles) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  char buf[160];
+  // the argument checks and messages of tsg_moe_group_pairs
+  if (query_count < 0) {
+    std::snprintf(buf, sizeof(buf), "queryCount must be non-negative, got %d", query_count);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (top_k <= 0) {
+    std::snprintf(buf, sizeof(buf), "topK must be positive, got %d", top_k);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (num_experts <= 0) {
+    std::snprintf(buf, sizeof(buf), "numExperts must be positive, got %d", num_experts);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (tile_expert_count < 1 || tile_expert_count > 16) {
+    std::snprintf(buf, sizeof(buf), "tileExpertCount must be in 1...16, got %d", tile_expert_count);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  if (sort_keys && n_sort_keys != num_experts) {
+    std::snprintf(buf, sizeof(buf), "expected %d expert sort keys, got %d", num_experts, n_sort_keys);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  const uint64_t expected = static_cast<uint64_t>(query_count) * static_cast<uint64_t>(top_k);
+  if (n_pairs != expected) {
+    std::snprintf(buf, sizeof(buf), "expected %llu route pairs, got %u",
+                  static_cast<unsigned long long>(expected), n_pairs);
+    return fail(ctx, TSG_ERR_INVALID_ARG, buf);
+  }
+  // the static scratch's limits
+  if (n_pairs > kGsPairs) {
+    std::snprintf(buf, sizeof(buf),
+                  "tsg_moe_group_pairs_noalloc: %u route pairs exceed its static scratch limit of "
+                  "%u pairs; use tsg_moe_group_pairs",
+                  n_pairs, static_cast<unsigned>(kGsPairs));
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, buf);
+  }
+  if (num_experts > static_cast<int32_t>(kGsExperts)) {
+    std::snprintf(buf, sizeof(buf),
+                  "tsg_moe_group_pairs_noalloc: %d experts exceed its static scratch limit of %u",
+                  num_experts, kGsExperts);
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, buf);
+  }
+  const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
+  if (tr < 16 || max_row_tiles(static_cast<uint32_t>(query_count), static_cast<uint32_t>(top_k),
+                               static_cast<uint32_t>(num_experts), tr) > kGsRowTiles)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE,
+                "tsg_moe_group_pairs_noalloc: row-tile schedule exceeds its static scratch");
+  if (n_pairs > 0 && (!pairs || !sorted_pairs)) return fail(ctx, TSG_ERR_INVALID_ARG, "null pairs");
+  if (!offsets || !counts || !groups || !n_groups || !tiles || !n_tiles)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "null output");
+
+  uint8_t* base = nullptr;
+  tsg_status st = group_scratch_on(ctx, &base);
+  if (st != TSG_OK) return st;
+  TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  if (n_pairs == 0) {
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(offsets, 0xFF, num_experts * 4u, ctx->stream), "memset");
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(counts, 0, num_experts * 4u, ctx->stream), "memset");
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(n_groups, 0, 4, ctx->stream), "memset");
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(n_tiles, 0, 4, ctx->stream), "memset");
+    return TSG_OK;
+  }
+  RouterParams p{};
+  p.T = query_count;
+  p.K = top_k;
+  p.E = num_experts;
+  p.tile_rows = static_cast<int>(tr);
+  p.tile_expert_count = tile_expert_count;
+  p.tile_break = tile_break;
+  p.sort_keys = sort_keys;
+  // Only the fields the permutation kernels touch; per-pair errors go to the
+  // context's status words, read back by tsg_sync as for tsg_moe_group_pairs.
+  RouteBuffers rb{};
+  rb.ids = reinterpret_cast<uint32_t*>(base + kGsOffIds);
+  rb.weights_f16 = reinterpret_cast<uint16_t*>(base + kGsOffW16);
+  rb.pair_pos = reinterpret_cast<uint32_t*>(base + kGsOffPos);
+  rb.row_tiles = reinterpret_cast<RowTile*>(base + kGsOffTiles);
+  rb.n_row_tiles = reinterpret_cast<uint32_t*>(base + kGsOffNTiles);
+  rb.sync_counter = reinterpret_cast<uint32_t*>(base + kGsOffCounter);
+  rb.err = ctx->status;
+  rb.sorted_pairs = reinterpret_cast<Pair*>(sorted_pairs);
+  rb.offsets = offsets;
+  rb.counts = counts;
+  rb.groups = reinterpret_cast<Group*>(groups);
+  rb.n_groups = n_groups;
+  rb.tiles = reinterpret_cast<Tile*>(tiles);
+  rb.n_tiles = n_tiles;
+  TSG_CUDA_TRY(ctx, launch_permute(p, rb, reinterpret_cast<const Pair*>(pairs), ctx->stream),
+               "group pairs (no-alloc)");
   return TSG_OK;
 }
 
