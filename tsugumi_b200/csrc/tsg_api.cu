@@ -61,12 +61,9 @@ struct tsg_ctx_s {
   __half* xp = nullptr;
   __half* partials = nullptr;
   // fused decode scratch
-  float* f_logits = nullptr;
-  void* f_xfrag = nullptr;
-  float* f_xsum = nullptr;
+  void* f_logits = nullptr;  // fused decode: tagged logits
+  size_t f_logits_bytes = 0;
   void* f_actfrag = nullptr;
-  float* f_actsum = nullptr;
-  float* f_vpart = nullptr;
   uint32_t* f_counters = nullptr;
   bool use_fused = true;
   bool allow_pdl = false;
@@ -136,6 +133,18 @@ uint32_t max_row_tiles(uint32_t T, uint32_t K, uint32_t E, uint32_t tile_rows) {
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Per-CTA launch epochs and gate/up flags of the fused decode kernel.
+constexpr size_t kFusedSignalBytes = 2 * 256 * sizeof(uint32_t);
+
+// Zeroes the fused decode kernel's signals (epochs, flags, tagged logits):
+// at allocation, and after a launch that reported an error, since such a
+// launch may leave CTAs at different epochs.
+cudaError_t reset_fused_signals(tsg_ctx ctx) {
+  cudaError_t e = cudaMemset(ctx->f_counters, 0, kFusedSignalBytes);
+  if (e == cudaSuccess && ctx->f_logits) e = cudaMemset(ctx->f_logits, 0, ctx->f_logits_bytes);
+  return e;
+}
+
 // Carves the workspace; with base == nullptr only returns the size.
 size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
   size_t off = 0;
@@ -178,20 +187,14 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
   // fused decode (T <= 4)
   const size_t Tf = std::min<size_t>(T, 4);
   const size_t rows_f = Tf * K + Tf;
-  float* f_logits = static_cast<float*>(take(Tf * (E + 1) * 4));
-  void* f_xfrag = take(Tf * D * 2);
-  float* f_xsum = static_cast<float*>(take(Tf * (D / 32) * 4));
+  // fused decode: (tag, logit) words in 4 copies, and the per-CTA signals
+  void* f_logits = take(4 * Tf * (E + 1) * 8);
   void* f_actfrag = take(rows_f * F * 2);
-  float* f_actsum = static_cast<float*>(take(rows_f * (F / 8) * 4));
-  float* f_vpart = static_cast<float*>(take(rows_f * D * 4));
-  uint32_t* f_counters = static_cast<uint32_t*>(take((4 + D / 16) * 4));
+  uint32_t* f_counters = static_cast<uint32_t*>(take(kFusedSignalBytes));
   if (base) {
     ctx->f_logits = f_logits;
-    ctx->f_xfrag = f_xfrag;
-    ctx->f_xsum = f_xsum;
+    ctx->f_logits_bytes = 4 * Tf * (E + 1) * 8;
     ctx->f_actfrag = f_actfrag;
-    ctx->f_actsum = f_actsum;
-    ctx->f_vpart = f_vpart;
     ctx->f_counters = f_counters;
     rb.sync_counter = ctx->status + 4;
     rb.err = ctx->status;
@@ -219,9 +222,8 @@ tsg_status ensure_workspace(tsg_ctx ctx, const Caps& want) {
   ctx->ws_bytes = bytes;
   ctx->caps = c;
   carve(ctx, c, static_cast<uint8_t*>(p));
-  // the fused decode kernel's counters must start at zero (they reset
-  // themselves at the end of every launch)
-  TSG_CUDA_TRY(ctx, cudaMemset(ctx->f_counters, 0, (4 + c.D / 16) * 4), "cudaMemset");
+  // the fused decode kernel's launch epochs, flags and tags start at zero
+  TSG_CUDA_TRY(ctx, reset_fused_signals(ctx), "cudaMemset");
   return TSG_OK;
 }
 
@@ -375,11 +377,7 @@ tsg_status run_decode_fused(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint
   a.residual = residual;
   a.logits = ctx->f_logits;
   a.inv_rms = ctx->rb.inv_rms;
-  a.xfrag = ctx->f_xfrag;
-  a.xsum = ctx->f_xsum;
   a.actfrag = ctx->f_actfrag;
-  a.actsum = ctx->f_actsum;
-  a.vpart = ctx->f_vpart;
   a.counters = ctx->f_counters;
   a.ids_out = ids_out;
   a.w_out = w_out;
@@ -400,7 +398,10 @@ tsg_status run_decode_fused(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint
 bool fused_ok(tsg_ctx ctx, const tsg_moe_layer_s* L, uint32_t T) {
   return ctx->use_fused &&
          decode_fused_supported(static_cast<int>(T), static_cast<int>(L->desc.top_k),
-                                static_cast<int>(L->desc.num_experts), L->has_gate, ctx->num_sms);
+                                static_cast<int>(L->desc.num_experts), L->has_gate, ctx->num_sms) &&
+         decode_fused_fits(static_cast<int>(T), static_cast<int>(L->desc.d),
+                           static_cast<int>(L->desc.f), static_cast<int>(L->desc.top_k),
+                           L->has_shared, ctx->num_sms);
 }
 
 tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
@@ -640,6 +641,7 @@ tsg_status tsg_sync(tsg_ctx ctx) {
   if (e != cudaSuccess) return cuda_fail(ctx, e, "status readback");
   if (st[0] == 0u) return TSG_OK;
   cudaMemset(ctx->status, 0, 4 * sizeof(uint32_t));
+  if (ctx->ws) reset_fused_signals(ctx);
   if (st[0] & TSG_DEVERR_TIMEOUT) {
     return fail(ctx, TSG_ERR_TIMEOUT, "a device-side wait ran out of time (pipeline fault)");
   }

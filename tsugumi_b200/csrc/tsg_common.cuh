@@ -112,9 +112,9 @@ TSG_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false (and flags TSG_DEVERR_TIMEOUT) when the limit runs out, or when
-// another thread of the launch has already flagged an error.
-TSG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+// another thread of the launch has already flagged an error.  The spin is
+// kept out of line so that every call site costs a few instructions of code.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, uint32_t* err) {
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
@@ -127,6 +127,10 @@ TSG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
     }
   }
   return true;
+}
+TSG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err);
 }
 
 // ---------------------------------------------------------------------------

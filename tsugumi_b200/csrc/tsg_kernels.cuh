@@ -143,13 +143,9 @@ struct DecodeFusedArgs {
   uint32_t y_stride;
   int y_f32;
   const float* residual;
-  float* logits;    // [T][E + 1]
+  void* logits;     // [4][T][E + 1] (tag, logit) words
   float* inv_rms;   // [T]
-  void* xfrag;      // [T][D] fp16, fragment order
-  float* xsum;      // [T][D / 32]
   void* actfrag;    // [T*K + T][F] fp16, fragment order
-  float* actsum;    // [T*K + T][F / 8]
-  float* vpart;     // [T*K + T][D]
   uint32_t* counters;  // [4 + D / 16], zero between launches
   uint32_t* ids_out;
   float* w_out;
@@ -161,7 +157,7 @@ struct DecodeFusedArgs {
   unsigned long long* stamps;  // debug phase timestamps [grid][8], or nullptr
 };
 bool decode_fused_supported(int T, int K, int E, int has_gate, int num_sms);
-size_t decode_fused_smem(int T, int D, int F, int K, int E, int has_gate, int num_sms);
+bool decode_fused_fits(int T, int D, int F, int K, int has_shared, int num_sms);
 cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t s);
 
 // umma.cu
