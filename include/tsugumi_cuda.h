@@ -280,6 +280,38 @@ TSG_API tsg_status tsg_last_routing(tsg_ctx ctx, const uint32_t **ids, const flo
                             const tsg_token_expert_pair **sorted_pairs, uint32_t *T,
                             uint32_t *K);
 
+/* ---- Expert parallelism across the GPUs of one node ----------------------
+ * No counterpart in the reference, which runs on one device: its per-layer
+ * sequence (RealForwardRunner.swift:1840-2640 prefill) is kept on each rank,
+ * with the experts split contiguously over R ranks.  Per layer, each rank
+ * routes its own tokens, exchanges per-expert pair counts, sends each
+ * normalised fp16 token row to the rank that owns its expert (NCCL
+ * all-to-all over NVLink), runs the grouped contraction on the rows it
+ * received (plus the shared expert on its own tokens), returns the expert
+ * outputs and combines its tokens in rank order -- the same arithmetic as one
+ * GPU, so the outputs are bit-equal.  NCCL (libnccl.so.2) is loaded when
+ * tsg_ep_init is first called. */
+#define TSG_EP_UNIQUE_ID_BYTES 128
+
+/* Writes a new NCCL unique id (TSG_EP_UNIQUE_ID_BYTES) on one rank; the
+ * caller hands it to every rank (e.g. over its own process group). */
+TSG_API tsg_status tsg_ep_unique_id(void *out_id);
+
+/* Joins the expert-parallel group: rank in [0, world), on ctx's device. */
+TSG_API tsg_status tsg_ep_init(tsg_ctx ctx, const void *unique_id, int rank, int world);
+
+/* The MoE block of T local tokens under expert parallelism.  `layer` holds
+ * this rank's experts: desc.num_experts is the global E (its router has all
+ * E rows), desc.experts points at the blob of expert `expert_first` =
+ * rank * E / world, and the blobs of the E / world local experts follow at
+ * expert_stride.  E must be a multiple of world.  Every rank calls this
+ * collectively, each with its own tokens (T may differ between ranks).
+ * Synchronises the context's stream once (after the count exchange). */
+TSG_API tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer layer, uint32_t expert_first,
+                                            const void *hidden_bf16, uint32_t hidden_stride,
+                                            uint32_t T, const float *residual_f32, void *y,
+                                            uint32_t y_stride, tsg_dtype y_dtype);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,8 @@
 // do, then enqueues kernels on the context's stream.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cstdio>
@@ -77,6 +79,21 @@ struct tsg_ctx_s {
   std::vector<cudaEvent_t> prof_events;
   uint32_t prof_max = 0, prof_calls = 0;
   bool profiling = false;
+  // expert parallelism
+  void* nccl_comm = nullptr;  // ncclComm_t
+  int ep_rank = 0, ep_world = 1;
+  size_t ep_rows_cap = 0;            // rows of ep_rows / ep_act / ep_out
+  __half* ep_rows = nullptr;         // received rows (+ own shared rows) [cap][D]
+  __half* ep_act = nullptr;          // [cap][F]
+  __half* ep_out = nullptr;          // local expert outputs [cap][D]
+  __half* ep_ret = nullptr;          // returned outputs in this rank's sorted order [cap][D]
+  size_t ep_ret_cap = 0;
+  uint32_t* ep_counts_recv = nullptr;  // [world][E / world] (device)
+  uint32_t* ep_h_counts = nullptr;     // pinned: [E] sent counts, then [world][E / world] received
+  RowTile* ep_tiles = nullptr;         // device row-tile schedule
+  RowTile* ep_h_tiles = nullptr;       // pinned staging
+  uint32_t* ep_ntiles = nullptr;       // device [1] (follows ep_tiles' capacity)
+  size_t ep_tiles_cap = 0;
 };
 
 struct tsg_moe_layer_s {
@@ -506,6 +523,81 @@ __global__ void fold_router_kernel(const float* w, const float* eff, const float
   }
 }
 
+// ---- NCCL, loaded on first use --------------------------------------------
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    auto sym = [&](const char* n) { return dlsym(h, n); };
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+    api.send = reinterpret_cast<decltype(api.send)>(sym("ncclSend"));
+    api.recv = reinterpret_cast<decltype(api.recv)>(sym("ncclRecv"));
+    api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
+    api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.send && api.recv &&
+             api.group_start && api.group_end && api.error_string;
+  });
+  return api;
+}
+
+tsg_status nccl_fail(tsg_ctx ctx, ncclResult_t r, const char* where) {
+  const NcclApi& n = nccl();
+  return fail(ctx, TSG_ERR_NCCL,
+              std::string(where) + ": " + (n.error_string ? n.error_string(r) : "NCCL error"));
+}
+
+#define TSG_NCCL_TRY(ctx, expr, where)                              \
+  do {                                                              \
+    ncclResult_t r__ = (expr);                                      \
+    if (r__ != ncclSuccess) return nccl_fail(ctx, r__, where);      \
+  } while (0)
+
+void release_ep(tsg_ctx ctx) {
+  if (ctx->nccl_comm && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(ctx->nccl_comm));
+  ctx->nccl_comm = nullptr;
+  for (void* p : {static_cast<void*>(ctx->ep_rows), static_cast<void*>(ctx->ep_act),
+                  static_cast<void*>(ctx->ep_out), static_cast<void*>(ctx->ep_ret),
+                  static_cast<void*>(ctx->ep_counts_recv), static_cast<void*>(ctx->ep_tiles)})
+    if (p) cudaFree(p);
+  if (ctx->ep_h_counts) cudaFreeHost(ctx->ep_h_counts);
+  if (ctx->ep_h_tiles) cudaFreeHost(ctx->ep_h_tiles);
+  ctx->ep_rows = ctx->ep_act = ctx->ep_out = ctx->ep_ret = nullptr;
+  ctx->ep_counts_recv = nullptr;
+  ctx->ep_tiles = nullptr;
+  ctx->ep_h_counts = nullptr;
+  ctx->ep_h_tiles = nullptr;
+  ctx->ep_rows_cap = ctx->ep_ret_cap = ctx->ep_tiles_cap = 0;
+}
+
+// Grows a device buffer of `n` elements of T (contents not kept).
+template <typename T>
+cudaError_t grow(T** p, size_t* cap, size_t need) {
+  if (*p && *cap >= need) return cudaSuccess;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(need, 1) * sizeof(T));
+  if (e == cudaSuccess) *cap = need;
+  return e;
+}
+
 }  // namespace
 
 // ---- scratch of tsg_moe_group_pairs_noalloc --------------------------------
@@ -598,6 +690,7 @@ tsg_status tsg_ctx_destroy(tsg_ctx ctx) {
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->status) cudaFree(ctx->status);
   for (cudaEvent_t e : ctx->prof_events) cudaEventDestroy(e);
+  release_ep(ctx);
   delete ctx;
   return TSG_OK;
 }
@@ -1190,6 +1283,249 @@ tsg_status tsg_last_routing(tsg_ctx ctx, const uint32_t** ids, const float** wei
   if (sorted_pairs) *sorted_pairs = reinterpret_cast<const tsg_token_expert_pair*>(ctx->rb.sorted_pairs);
   if (T) *T = ctx->last_T;
   if (K) *K = ctx->last_K;
+  return TSG_OK;
+}
+
+// ---- expert parallelism ------------------------------------------------------
+
+tsg_status tsg_ep_unique_id(void* out_id) {
+  if (!out_id) return TSG_ERR_INVALID_ARG;
+  static_assert(sizeof(ncclUniqueId) == TSG_EP_UNIQUE_ID_BYTES, "NCCL unique id size");
+  const NcclApi& n = nccl();
+  if (!n.ok) return TSG_ERR_NCCL;
+  ncclUniqueId id;
+  if (n.get_unique_id(&id) != ncclSuccess) return TSG_ERR_NCCL;
+  std::memcpy(out_id, &id, sizeof(id));
+  return TSG_OK;
+}
+
+tsg_status tsg_ep_init(tsg_ctx ctx, const void* unique_id, int rank, int world) {
+  if (!ctx) return TSG_ERR_INVALID_ARG;
+  if (!unique_id || world < 1 || rank < 0 || rank >= world)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "expert-parallel group: bad unique id, rank or world");
+  if (ctx->nccl_comm) return fail(ctx, TSG_ERR_INVALID_ARG, "context already joined a group");
+  const NcclApi& n = nccl();
+  if (!n.ok) return fail(ctx, TSG_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  ncclComm_t comm = nullptr;
+  TSG_NCCL_TRY(ctx, n.comm_init_rank(&comm, world, id, rank), "ncclCommInitRank");
+  ctx->nccl_comm = comm;
+  ctx->ep_rank = rank;
+  ctx->ep_world = world;
+  return TSG_OK;
+}
+
+tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t expert_first,
+                                    const void* hidden, uint32_t hidden_stride, uint32_t T,
+                                    const float* residual, void* y, uint32_t y_stride,
+                                    tsg_dtype y_dtype) {
+  tsg_status st = check_common(ctx, L, hidden, hidden_stride, T, y, y_stride, y_dtype);
+  if (st != TSG_OK) return st;
+  if (!ctx->nccl_comm) return fail(ctx, TSG_ERR_INVALID_ARG, "tsg_ep_init has not been called");
+  const int R = ctx->ep_world, rank = ctx->ep_rank;
+  const uint32_t E = L->desc.num_experts, K = L->desc.top_k, D = L->desc.d, F = L->desc.f;
+  if (E % static_cast<uint32_t>(R))
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "numExperts must be a multiple of the group size");
+  const uint32_t El = E / static_cast<uint32_t>(R);
+  if (expert_first != static_cast<uint32_t>(rank) * El)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "expert_first must be rank * numExperts / world");
+  st = take_pending_error(ctx);
+  if (st != TSG_OK) return st;
+  st = ensure_workspace(ctx, layer_caps(L, std::max<uint32_t>(T, 1)));
+  if (st != TSG_OK) return st;
+  const NcclApi& n = nccl();
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
+  cudaStream_t s = ctx->stream;
+  RouteBuffers& rb = ctx->rb;
+  const uint32_t P = T * K;
+  const uint32_t shared_rows = L->has_shared ? T : 0u;
+  ctx->last_T = T;
+  ctx->last_K = K;
+
+  // 1. route and group this rank's tokens over all E experts: the sorted
+  //    order puts the pairs of each owner rank in one contiguous run
+  if (T > 0) {
+    const RouterParams p = router_params(L, hidden, hidden_stride, T);
+    TSG_CUDA_TRY(ctx, launch_router_prefill(p, rb, s), "router");
+    TSG_CUDA_TRY(ctx, launch_permute(p, rb, nullptr, s), "permute");
+    const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(E) * D : nullptr;
+    TSG_CUDA_TRY(ctx,
+                 launch_gather_rows_gate(static_cast<const uint16_t*>(hidden), hidden_stride,
+                                         rb.inv_rms, rb.sorted_pairs, static_cast<int>(P),
+                                         static_cast<int>(T), static_cast<int>(D), L->has_shared,
+                                         ctx->xp, gate_w, rb.gate_raw, s),
+                 "gather rows");
+  } else {
+    TSG_CUDA_TRY(ctx, cudaMemsetAsync(rb.counts, 0, E * 4u, s), "memset");
+  }
+
+  // 2. per-expert pair counts to the experts' owners; the host needs them
+  //    to size the row exchange
+  if (!ctx->ep_counts_recv) {
+    TSG_CUDA_TRY(ctx, cudaMalloc(&ctx->ep_counts_recv, 512 * sizeof(uint32_t)), "cudaMalloc");
+    TSG_CUDA_TRY(ctx, cudaHostAlloc(&ctx->ep_h_counts, 2 * 512 * sizeof(uint32_t),
+                                    cudaHostAllocDefault), "cudaHostAlloc");
+  }
+  TSG_NCCL_TRY(ctx, n.group_start(), "ncclGroupStart");
+  for (int q = 0; q < R; ++q) {
+    TSG_NCCL_TRY(ctx, n.send(rb.counts + q * El, El, ncclUint32, q, comm, s), "ncclSend(counts)");
+    TSG_NCCL_TRY(ctx, n.recv(ctx->ep_counts_recv + q * El, El, ncclUint32, q, comm, s),
+                 "ncclRecv(counts)");
+  }
+  TSG_NCCL_TRY(ctx, n.group_end(), "ncclGroupEnd");
+  uint32_t* hc = ctx->ep_h_counts;
+  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(hc, rb.counts, E * 4u, cudaMemcpyDeviceToHost, s), "counts");
+  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(hc + E, ctx->ep_counts_recv, E * 4u, cudaMemcpyDeviceToHost, s),
+               "counts");
+  TSG_CUDA_TRY(ctx, cudaStreamSynchronize(s), "cudaStreamSynchronize");
+
+  // 3. the plan: send/receive runs per peer, and the local row tiles -- one
+  //    run per (source rank, local expert), then the shared expert's rows
+  std::vector<uint32_t> send_cnt(R), send_off(R), recv_cnt(R), recv_off(R);
+  uint32_t so = 0, ro = 0;
+  for (int q = 0; q < R; ++q) {
+    uint32_t sc = 0, rc = 0;
+    for (uint32_t j = 0; j < El; ++j) {
+      sc += hc[q * El + j];
+      rc += hc[E + q * El + j];
+    }
+    send_cnt[q] = sc;
+    send_off[q] = so;
+    recv_cnt[q] = rc;
+    recv_off[q] = ro;
+    so += sc;
+    ro += rc;
+  }
+  if (so != P) return fail(ctx, TSG_ERR_CUDA, "expert-parallel: pair counts do not add up");
+  const uint32_t recv_rows = ro;
+  const uint32_t rows_local = recv_rows + shared_rows;
+  const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
+  std::vector<RowTile> tiles;
+  for (int q = 0; q < R; ++q) {
+    uint32_t off = recv_off[q];
+    for (uint32_t j = 0; j < El; ++j) {
+      const uint32_t c = hc[E + q * El + j];
+      for (uint32_t b = 0; b < c; b += tr) tiles.push_back({j, off + b, std::min(tr, c - b), 0});
+      off += c;
+    }
+  }
+  for (uint32_t b = 0; b < shared_rows; b += tr)
+    tiles.push_back({El, recv_rows + b, std::min(tr, shared_rows - b), 0});
+  const uint32_t n_tiles = static_cast<uint32_t>(tiles.size());
+
+  // (the stream is idle here, so buffers can be replaced)
+  if (rows_local > ctx->ep_rows_cap || static_cast<size_t>(D) * ctx->ep_rows_cap == 0) {
+    const size_t rows = std::max<size_t>(rows_local + rows_local / 4, 1024);
+    size_t c1 = 0, c2 = 0, c3 = 0;
+    ctx->ep_rows_cap = 0;
+    TSG_CUDA_TRY(ctx, grow(&ctx->ep_rows, &c1, rows * D), "cudaMalloc");
+    TSG_CUDA_TRY(ctx, grow(&ctx->ep_act, &c2, rows * F), "cudaMalloc");
+    TSG_CUDA_TRY(ctx, grow(&ctx->ep_out, &c3, rows * D), "cudaMalloc");
+    ctx->ep_rows_cap = rows;
+  }
+  TSG_CUDA_TRY(ctx, grow(&ctx->ep_ret, &ctx->ep_ret_cap, static_cast<size_t>(P + shared_rows) * D),
+               "cudaMalloc");
+  if (!ctx->ep_tiles || ctx->ep_tiles_cap < n_tiles + 1) {
+    if (ctx->ep_tiles) cudaFree(ctx->ep_tiles);
+    if (ctx->ep_h_tiles) cudaFreeHost(ctx->ep_h_tiles);
+    ctx->ep_tiles = nullptr;
+    ctx->ep_h_tiles = nullptr;
+    const size_t cap = std::max<size_t>(2 * (n_tiles + 1), 256);
+    TSG_CUDA_TRY(ctx, cudaMalloc(&ctx->ep_tiles, (cap + 1) * sizeof(RowTile)), "cudaMalloc");
+    TSG_CUDA_TRY(ctx, cudaHostAlloc(&ctx->ep_h_tiles, (cap + 1) * sizeof(RowTile),
+                                    cudaHostAllocDefault), "cudaHostAlloc");
+    ctx->ep_tiles_cap = cap;
+  }
+  // the tile count rides in the slot after the tiles
+  RowTile* ht = ctx->ep_h_tiles;
+  std::copy(tiles.begin(), tiles.end(), ht);
+  ht[ctx->ep_tiles_cap].expert = n_tiles;
+  ctx->ep_ntiles = &ctx->ep_tiles[ctx->ep_tiles_cap].expert;
+  if (n_tiles)
+    TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_tiles, ht, n_tiles * sizeof(RowTile),
+                                      cudaMemcpyHostToDevice, s), "tiles");
+  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_ntiles, &ht[ctx->ep_tiles_cap].expert, sizeof(uint32_t),
+                                    cudaMemcpyHostToDevice, s), "tiles");
+
+  // 4. dispatch: each owner receives its rows, run after run
+  const size_t rowb = D;  // elements per row
+  TSG_NCCL_TRY(ctx, n.group_start(), "ncclGroupStart");
+  for (int q = 0; q < R; ++q) {
+    if (send_cnt[q])
+      TSG_NCCL_TRY(ctx, n.send(ctx->xp + send_off[q] * rowb, send_cnt[q] * rowb, ncclFloat16, q,
+                               comm, s), "ncclSend(rows)");
+    if (recv_cnt[q])
+      TSG_NCCL_TRY(ctx, n.recv(ctx->ep_rows + recv_off[q] * rowb, recv_cnt[q] * rowb, ncclFloat16,
+                               q, comm, s), "ncclRecv(rows)");
+  }
+  TSG_NCCL_TRY(ctx, n.group_end(), "ncclGroupEnd");
+  if (shared_rows)
+    TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_rows + recv_rows * rowb, ctx->xp + P * rowb,
+                                      shared_rows * rowb * 2, cudaMemcpyDeviceToDevice, s),
+                 "shared rows");
+
+  // 5. the grouped contraction over the rows this rank holds
+  if (n_tiles) {
+    CUtensorMap maps[2];
+    if (!encode_rows_map(&maps[0], ctx->ep_rows, rows_local, D) ||
+        !encode_rows_map(&maps[1], ctx->ep_act, rows_local, F))
+      return fail(ctx, TSG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    QmmParams qp{};
+    qp.D = static_cast<int>(D);
+    qp.F = static_cast<int>(F);
+    qp.E = static_cast<int>(El);
+    qp.act = static_cast<int>(L->desc.activation);
+    qp.n_rows_total = static_cast<int>(rows_local);
+    qp.experts = expert_set(L);
+    qp.row_tiles = ctx->ep_tiles;
+    qp.n_row_tiles = ctx->ep_ntiles;
+    qp.xp = ctx->ep_rows;
+    qp.act_buf = ctx->ep_act;
+    qp.partials = ctx->ep_out;
+    qp.err = rb.err;
+    qp.num_sms = ctx->num_sms;
+    qp.maps = maps;
+    TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, s), "qmm gate/up");
+    TSG_CUDA_TRY(ctx, launch_qmm_down(qp, s), "qmm down");
+  }
+
+  // 6. return the outputs to the tokens' ranks, into their sorted positions
+  TSG_NCCL_TRY(ctx, n.group_start(), "ncclGroupStart");
+  for (int q = 0; q < R; ++q) {
+    if (recv_cnt[q])
+      TSG_NCCL_TRY(ctx, n.send(ctx->ep_out + recv_off[q] * rowb, recv_cnt[q] * rowb, ncclFloat16,
+                               q, comm, s), "ncclSend(outputs)");
+    if (send_cnt[q])
+      TSG_NCCL_TRY(ctx, n.recv(ctx->ep_ret + send_off[q] * rowb, send_cnt[q] * rowb, ncclFloat16,
+                               q, comm, s), "ncclRecv(outputs)");
+  }
+  TSG_NCCL_TRY(ctx, n.group_end(), "ncclGroupEnd");
+  if (shared_rows)
+    TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_ret + P * rowb, ctx->ep_out + recv_rows * rowb,
+                                      shared_rows * rowb * 2, cudaMemcpyDeviceToDevice, s),
+                 "shared outputs");
+
+  // 7. combine this rank's tokens, ranks in order (as on one GPU)
+  if (T > 0) {
+    CombineParams cp{};
+    cp.T = static_cast<int>(T);
+    cp.D = static_cast<int>(D);
+    cp.K = static_cast<int>(K);
+    cp.has_shared = L->has_shared;
+    cp.E = static_cast<int>(E);
+    cp.partials = ctx->ep_ret;
+    cp.pair_pos = rb.pair_pos;
+    cp.weights = rb.weights;
+    cp.gate_raw = L->has_gate ? rb.gate_raw : nullptr;
+    cp.inv_rms = rb.inv_rms;
+    cp.residual = residual;
+    cp.y = y;
+    cp.y_stride = y_stride;
+    cp.y_f32 = y_dtype == TSG_DTYPE_F32 ? 1 : 0;
+    TSG_CUDA_TRY(ctx, launch_combine(cp, s), "combine");
+  }
   return TSG_OK;
 }
 
