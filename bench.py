@@ -318,6 +318,7 @@ def run_ours(args):
             sweep.update(run_decode_sweep(ctx, layers, device, args, barrier))
         except Exception as exc:
             sweep["decode_sweep_error"] = repr(exc)
+        sweep.update(run_ep_sweep(device, args, rank, world, local))
 
     result = {
         "metric": METRIC,
@@ -392,6 +393,75 @@ def run_decode_sweep(ctx, layers, device, args, barrier):
         out[f"decode_T{T}"] = {"layer_tokens_per_s": T * LAYERS / (ms / 1e3), "ms_per_step": ms,
                                "u_mean": float(np.mean(us)), "expert_gbs": gbs,
                                "hbm_frac": gbs / pk["hbm_gbs"]}
+    return out
+
+
+def run_ep_sweep(device, args, rank, world, local):
+    """32768 tokens with Zipf(1.1) routing skew spread evenly over
+    the ranks; at N > 1 through expert parallelism (experts split contiguously,
+    NCCL all-to-all), at N = 1 through the single-GPU prefill path, so that
+    the ratio between the two is the expert-parallel speed-up.  Two seeded
+    layers of each of the Gemma-like and Qwen-like shapes; the time per layer
+    is the maximum over ranks (CUDA events between barriers)."""
+    import torch
+    import torch.distributed as dist
+    import tsugumi_b200 as tb
+    from tsugumi_b200 import ep
+    from tsugumi_b200.synthetic import device_layer_tensors
+
+    total = 32768
+    T = total // world
+    out = {}
+    ctx = tb.Context(local)
+    ctx.set_stream(torch.cuda.current_stream())
+    group = ep.ExpertParallelGroup.from_torch_distributed(ctx) if world > 1 else None
+    for name in ("gemma", "qwen"):
+        tensors = [device_layer_tensors(name, 5150 + 31 * l, 1.1, device) for l in range(2)]
+        if group is not None:
+            lays = [ep.EPMoELayer(group, t) for t in tensors]
+        else:
+            lays = [tb.MoELayer(ctx, t) for t in tensors]
+        d = tensors[0]["d"]
+        g = torch.Generator(device=device)
+        g.manual_seed(9000 + rank)
+        x = torch.randn((T, d), generator=g, device=device).to(torch.bfloat16)
+        y = torch.empty((T, d), dtype=torch.bfloat16, device=device)
+        if group is None:
+            ctx.reserve(lays[0], T)
+        for _ in range(2):
+            for lay in lays:
+                lay.forward(x, y=y)
+        torch.cuda.synchronize()
+        steps = 3
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            for lay in lays:
+                lay.forward(x, y=y)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (steps * len(lays))
+        t = torch.tensor([ms], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        f = tensors[0]["f"]
+        k = tensors[0]["top_k"]
+        flops = 2.0 * total * k * 3 * d * f
+        out[f"ep_prefill_{name}"] = {
+            "world": world, "tokens": total, "tokens_per_rank": T,
+            "ms_per_layer": ms, "layer_tokens_per_s": total / (ms / 1e3),
+            "routed_tflops": flops / (ms / 1e3) / 1e12,
+            "path": "expert parallel (NCCL all-to-all)" if group is not None
+                    else "single GPU prefill"}
+        for lay in lays:
+            lay.close()
+        del lays, tensors
+        torch.cuda.empty_cache()
+    ctx.close()
     return out
 
 
