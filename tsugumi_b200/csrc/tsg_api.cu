@@ -104,14 +104,7 @@ struct tsg_moe_layer_s {
   int has_shared = 0;
 };
 
-namespace {
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_tiled_fn() {
+EncodeTiledFn tsg::encode_tiled_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -124,6 +117,8 @@ EncodeTiledFn encode_tiled_fn() {
   });
   return fn;
 }
+
+namespace {
 
 tsg_status fail(tsg_ctx ctx, tsg_status st, const std::string& msg) {
   if (ctx) ctx->last_error = msg;
@@ -287,17 +282,6 @@ ExpertSet expert_set(const tsg_moe_layer_s* L) {
   return s;
 }
 
-bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
-  EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {64, 16};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 // Records stage boundary `k` (0..4) of the current profiled call.  Inside
 // stream capture the record must be "external" to become a graph node that
@@ -439,10 +423,6 @@ tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, u
                                        ctx->stream),
                "gather rows");
   const uint32_t rows = P + (L->has_shared ? T : 0u);
-  CUtensorMap maps[2];
-  if (!encode_rows_map(&maps[0], ctx->xp, rows, L->desc.d) ||
-      !encode_rows_map(&maps[1], ctx->act_buf, rows, L->desc.f))
-    return fail(ctx, TSG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   QmmParams qp{};
   qp.D = static_cast<int>(L->desc.d);
   qp.F = static_cast<int>(L->desc.f);
@@ -457,7 +437,6 @@ tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, u
   qp.partials = ctx->partials;
   qp.err = ctx->rb.err;
   qp.num_sms = ctx->num_sms;
-  qp.maps = maps;
   prof_mark(ctx, 1);
   TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, ctx->stream), "qmm gate/up");
   prof_mark(ctx, 2);
@@ -1237,10 +1216,6 @@ tsg_status tsg_shared_expert(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32
                                        static_cast<int>(L->desc.d), 1, ctx->xp, gate_w,
                                        rb.gate_raw, ctx->stream),
                "gather");
-  CUtensorMap maps[2];
-  if (!encode_rows_map(&maps[0], ctx->xp, T, L->desc.d) ||
-      !encode_rows_map(&maps[1], ctx->act_buf, T, L->desc.f))
-    return fail(ctx, TSG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   QmmParams qp{};
   qp.D = static_cast<int>(L->desc.d);
   qp.F = static_cast<int>(L->desc.f);
@@ -1255,7 +1230,6 @@ tsg_status tsg_shared_expert(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32
   qp.partials = ctx->partials;
   qp.err = rb.err;
   qp.num_sms = ctx->num_sms;
-  qp.maps = maps;
   TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, ctx->stream), "qmm gate/up");
   TSG_CUDA_TRY(ctx, launch_qmm_down(qp, ctx->stream), "qmm down");
   CombineParams cp{};
@@ -1468,10 +1442,6 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
 
   // 5. the grouped contraction over the rows this rank holds
   if (n_tiles) {
-    CUtensorMap maps[2];
-    if (!encode_rows_map(&maps[0], ctx->ep_rows, rows_local, D) ||
-        !encode_rows_map(&maps[1], ctx->ep_act, rows_local, F))
-      return fail(ctx, TSG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     QmmParams qp{};
     qp.D = static_cast<int>(D);
     qp.F = static_cast<int>(F);
@@ -1486,7 +1456,6 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
     qp.partials = ctx->ep_out;
     qp.err = rb.err;
     qp.num_sms = ctx->num_sms;
-    qp.maps = maps;
     TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, s), "qmm gate/up");
     TSG_CUDA_TRY(ctx, launch_qmm_down(qp, s), "qmm down");
   }

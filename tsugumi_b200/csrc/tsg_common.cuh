@@ -133,6 +133,38 @@ TSG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
   return mbar_wait_slow(bar, parity, err);
 }
 
+// As mbar_wait, but each try suspends the thread in hardware (up to
+// kSuspendHintNs, or until the phase completes) instead of spinning, so a
+// warp that waits for a long time takes no issue slots from the warps that
+// work.  For pipelines with many waiting warps per SM.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+TSG_DEV bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0u;
+}
+static __device__ __noinline__ bool mbar_sleep_slow(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait_suspend(bar, parity)) {
+    if (error_raised(err)) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      flag_error(err, TSG_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+TSG_DEV bool mbar_sleep(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_sleep_slow(bar, parity, err);
+}
+
 // ---------------------------------------------------------------------------
 // Bulk (1-D) and tensor (TMA) copies, global -> shared, no multicast.
 // ---------------------------------------------------------------------------
@@ -208,6 +240,43 @@ TSG_DEV void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T.  A is M=128 rows in TMEM lanes 0-127,
+// K packed two fp16 per 32-bit column (element 2c in the low half of column
+// c), so one K=16 step reads 8 columns from `a_tmem`.
+TSG_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// One 64-wide k-step as four K=16 MMAs issued from a single asm block, A in
+// TMEM (columns a_tmem, +8, +16, +24) and B in a 128-byte-swizzled smem tile
+// (descriptor b_desc, advanced by 32 bytes per K=16).  Issuing the four with
+// their operands already in distinct registers lets them leave the issuing
+// thread back to back; issued one by one with address arithmetic in between,
+// each waits for the previous one's operands to be consumed.
+TSG_DEV void umma_f16_ts_k64(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                             uint32_t accumulate) {
+  const uint64_t b1 = b_desc + 2u, b2 = b_desc + 4u, b3 = b_desc + 6u;
+  asm volatile(
+      "{\n\t.reg .pred p0, p1;\n\t.reg .b32 a1, a2, a3;\n\t"
+      "setp.ne.b32 p0, %4, 0;\n\t"
+      "setp.eq.b32 p1, %4, %4;\n\t"
+      "add.u32 a1, %1, 8;\n\t"
+      "add.u32 a2, %1, 16;\n\t"
+      "add.u32 a3, %1, 24;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], %5, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], %6, %3, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], %7, %3, p1;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "l"(b1), "l"(b2), "l"(b3)
+      : "memory");
+}
+
 // Arrive on an mbarrier once every UMMA issued so far by this thread is done.
 TSG_DEV void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -228,6 +297,19 @@ TSG_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "memory");
 }
 TSG_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// The store counterpart: 16 consecutive columns of this thread's lane.  The
+// warp may only address its own lane quarter (32 * (warp % 4)).
+TSG_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+TSG_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand tile stored in the
 // 128-byte swizzle layout: rows of 128 bytes (64 fp16 of K), 8-row atoms of
@@ -306,6 +388,18 @@ TSG_DEV float gelu_tanh_f(float x) {
   return 0.5f * x * (1.0f + tanhf(inner));
 }
 TSG_DEV float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// The same two activations for epilogues that evaluate thousands per
+// thread: 0.5 x (1 + tanh(y)) = x / (1 + exp(-2y)) exactly, evaluated with
+// the hardware exponential and a fast divide (relative error ~1e-6, far
+// below the fp16 rounding of the result).  exp overflowing to +inf for very
+// negative x gives x / inf = -0, the limit.
+TSG_DEV float gelu_tanh_fast(float x) {
+  const float y = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return __fdividef(x, 1.0f + __expf(-2.0f * y));
+}
+TSG_DEV float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+TSG_DEV float gate_act_fast(int act, float g) { return act == 1 ? silu_fast(g) : gelu_tanh_fast(g); }
 TSG_DEV float gate_act(int act, float g) { return act == 1 ? silu_f(g) : gelu_tanh_f(g); }
 
 TSG_DEV float warp_sum(float v) {

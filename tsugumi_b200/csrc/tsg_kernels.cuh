@@ -8,6 +8,14 @@
 
 namespace tsg {
 
+// cuTensorMapEncodeTiled, found once through the runtime's driver entry
+// point query (nullptr when the driver does not offer it).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
 // Byte offsets of an expert's sub-tensors inside its blob (MoEExpertOffsets,
 // Sources/Tsugumi/Kernels/MoE/MoE.swift:4-29).  Bias offsets are carried
 // for layout compatibility and never read: the scheme is symmetric.
@@ -172,8 +180,10 @@ struct QmmParams {
   __half* partials;      // [rows, D] fp16 (GEMM2 output)
   uint32_t* err;
   int num_sms;
-  const CUtensorMap* maps;  // host copies: [0] xp rows, [1] act rows
 };
+// The launchers encode their own tensor maps (token rows of xp / act_buf,
+// int4 code planes of the routed and shared experts); a failed encode is
+// reported as cudaErrorInvalidValue.
 cudaError_t launch_qmm_gate_up(const QmmParams& p, cudaStream_t s);
 cudaError_t launch_qmm_down(const QmmParams& p, cudaStream_t s);
 int qmm_tile_rows();
