@@ -2,18 +2,21 @@
 //
 // Restates PrefillMoEGrouping.groupTokenExpertPairs
 // (Sources/Tsugumi/Kernels/Prefill/MoE/PrefillMoEGrouping.swift:91-201), which
-// the reference runs on the CPU, as three kernels:
-//   1. (caller-supplied pairs only) validate each pair and place it at its
+// the reference runs on the CPU, as a stable counting sort over the
+// token-major pairs, in chunks of kChunk pairs:
+//   0. (caller-supplied pairs only) validate each pair and place it at its
 //      token-major slot token*K + rank; a second pair for the same slot is a
 //      duplicate (PrefillMoEGroupingError.duplicateTokenRank);
-//   2. one CTA per expert counts its pairs; the last CTA to finish orders the
-//      experts (by optional sort key, then index), scans the counts into
-//      offsets (UINT32_MAX for empty experts), and writes the groups, the
-//      tiles of <= tileExpertCount groups (with the optional forced cut) and
-//      the row-tile schedule of the grouped contraction;
-//   3. one CTA per expert walks the token-major pairs in order and writes its
-//      pairs to consecutive sorted positions with block-wide ballots, so the
-//      order inside an expert is (token, rank) -- a stable counting sort.
+//   1. one CTA per chunk histograms its expert ids in shared memory;
+//   2. one CTA turns the histograms into per-(chunk, expert) prefixes and the
+//      per-expert counts, orders the experts (by optional sort key, then
+//      index), scans the counts into offsets (UINT32_MAX for empty experts),
+//      and writes the groups, the tiles of <= tileExpertCount groups (with
+//      the optional forced cut) and the row-tile schedule of the grouped
+//      contraction;
+//   3. one CTA per chunk writes its pairs to their sorted positions, ranking
+//      equal ids inside a warp with match/popc and across warps with
+//      per-warp counts, so the order inside an expert is (token, rank).
 // Output is bit-identical to the reference's sort by (key, expert, token,
 // rank).
 #include "tsg_common.cuh"
@@ -23,6 +26,8 @@ namespace tsg {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kChunk = 2048;       // pairs per histogram / scatter CTA
+constexpr int kScanThreads = 512;
 
 // Error record: [0] bits, [1] first error code, [2] offending value.
 TSG_DEV void record_error(uint32_t* err, uint32_t code, uint32_t value) {
@@ -100,33 +105,45 @@ struct PermuteArgs {
   const uint64_t* sort_keys;
 };
 
-__global__ void __launch_bounds__(kThreads) permute_count_kernel(PermuteArgs a, RouteBuffers rb) {
-  __shared__ uint32_t s_tmp[33];
-  __shared__ uint32_t s_last;
-  extern __shared__ uint32_t s_dyn[];  // [3 * E] in the last CTA
-  const int e = blockIdx.x;
-  uint32_t cnt = 0;
-  for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
+// ---- 1. per-chunk histograms -------------------------------------------------
+__global__ void __launch_bounds__(kThreads) permute_hist_kernel(PermuteArgs a, RouteBuffers rb) {
+  extern __shared__ uint32_t s_h[];  // [E]
+  const int c = blockIdx.x;
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) s_h[e] = 0u;
+  __syncthreads();
+  const int end = min(a.P, (c + 1) * kChunk);
+  for (int i = c * kChunk + threadIdx.x; i < end; i += blockDim.x) {
     const uint32_t id = a.tm_ids[i];
-    cnt += (id == static_cast<uint32_t>(e)) ? 1u : 0u;
-    if (e == 0 && id >= static_cast<uint32_t>(a.E)) record_error(rb.err, 8u, id);
+    if (id < static_cast<uint32_t>(a.E)) atomicAdd(&s_h[id], 1u);
+    else record_error(rb.err, 8u, id);
   }
-  const uint32_t total = block_sum_u32(cnt, s_tmp);
-  if (threadIdx.x == 0) rb.counts[e] = total;
-
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(rb.sync_counter, 1u) == gridDim.x - 1) ? 1u : 0u;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (threadIdx.x == 0) *rb.sync_counter = 0u;
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x)
+    rb.hist[static_cast<size_t>(c) * a.E + e] = s_h[e];
+}
 
+// ---- 2. prefixes, counts, expert order, groups and schedules ----------------
+__global__ void __launch_bounds__(kScanThreads) permute_scan_kernel(PermuteArgs a, RouteBuffers rb,
+                                                                    int n_chunks) {
+  __shared__ uint32_t s_tmp[33];
+  extern __shared__ uint32_t s_dyn[];  // [3 * E]
+  uint32_t* s_cnt = s_dyn;  // [E]
+  // each thread turns one expert's column of chunk counts into prefixes
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+    uint32_t run = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+      uint32_t* h = rb.hist + static_cast<size_t>(c) * a.E + e;
+      const uint32_t v = *h;
+      *h = run;
+      run += v;
+    }
+    s_cnt[e] = run;
+    rb.counts[e] = run;
+  }
+  __syncthreads();
   const int E = a.E;
-  uint32_t* s_cnt = s_dyn;          // [E]
   uint32_t* s_order = s_dyn + E;    // [E] order position -> expert
   uint32_t* s_rank = s_dyn + 2 * E; // [E] expert -> order position
-  for (int x = threadIdx.x; x < E; x += blockDim.x) s_cnt[x] = __ldcg(rb.counts + x);
   // order experts by (sort key, index): rank = number of experts before it
   for (int x = threadIdx.x; x < E; x += blockDim.x) {
     uint32_t r = static_cast<uint32_t>(x);
@@ -214,28 +231,57 @@ __global__ void __launch_bounds__(kThreads) permute_count_kernel(PermuteArgs a, 
 __global__ void __launch_bounds__(kThreads) permute_scatter_kernel(PermuteArgs a, RouteBuffers rb,
                                                                   const uint16_t* tm_w16,
                                                                   const float* w_f32) {
-  __shared__ uint32_t s_tmp[33];
-  const int e = blockIdx.x;
-  const uint32_t count = __ldcg(rb.counts + e);
-  if (count == 0u) return;
-  uint32_t run = __ldcg(rb.offsets + e);
-  for (int base = 0; base < a.P; base += blockDim.x) {
-    const int i = base + threadIdx.x;
-    const bool hit = i < a.P && a.tm_ids[i] == static_cast<uint32_t>(e);
-    uint32_t tot;
-    const uint32_t pre = block_excl_scan(hit ? 1u : 0u, s_tmp, &tot);
-    if (hit) {
-      const uint32_t pos = run + pre;
+  extern __shared__ uint32_t s_dyn[];
+  const int E = a.E;
+  uint32_t* s_base = s_dyn;          // [E] sorted position of this chunk's first pair of e
+  uint32_t* s_run = s_dyn + E;       // [E] pairs of e already placed by this chunk
+  uint32_t* s_wc = s_dyn + 2 * E;    // [kThreads / 32][E] per-warp counts of the sub-block
+  const int c = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kThreads / 32;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const uint32_t off = __ldcg(rb.offsets + e);
+    s_base[e] = off + rb.hist[static_cast<size_t>(c) * E + e];  // unused when e is empty
+    s_run[e] = 0u;
+  }
+  for (int x = threadIdx.x; x < kWarps * E; x += blockDim.x) s_wc[x] = 0u;
+  __syncthreads();
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  const int end = min(a.P, (c + 1) * kChunk);
+  for (int sb = c * kChunk; sb < end; sb += kThreads) {
+    const int i = sb + static_cast<int>(threadIdx.x);
+    const uint32_t raw = i < end ? a.tm_ids[i] : 0xFFFFFFFFu;
+    const bool valid = raw < static_cast<uint32_t>(E);
+    const uint32_t id = valid ? raw : 0xFFFFFFFFu;
+    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, id);
+    const uint32_t lt = __popc(peers & lt_mask);
+    const uint32_t cnt_w = __popc(peers);
+    if (valid && lt == 0u) s_wc[warp * E + id] = cnt_w;
+    __syncthreads();
+    uint32_t rank = 0;
+    bool last = false;
+    if (valid) {
+      uint32_t pre = 0, later = 0;
+      for (int w = 0; w < kWarps; ++w) {
+        const uint32_t v = s_wc[w * E + id];
+        pre += w < warp ? v : 0u;
+        later += w > warp ? v : 0u;
+      }
+      rank = s_run[id] + pre + lt;
+      last = (lt == cnt_w - 1u) && later == 0u;
+      const uint32_t pos = s_base[id] + rank;
       Pair pr;
       pr.token = static_cast<uint32_t>(i / a.K);
-      pr.expert = static_cast<uint32_t>(e);
+      pr.expert = id;
       pr.rank = static_cast<uint32_t>(i % a.K);
       pr.weight_bits = tm_w16 ? tm_w16[i] : __half_as_ushort(__float2half_rn(w_f32[i]));
       rb.sorted_pairs[pos] = pr;
       rb.pair_pos[i] = pos;
     }
-    run += tot;
-    if (run - __ldcg(rb.offsets + e) >= count) break;
+    __syncthreads();
+    if (last) s_run[id] = rank + 1u;
+    if (valid && lt == 0u) s_wc[warp * E + id] = 0u;
+    __syncthreads();
   }
 }
 
@@ -297,6 +343,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, uin
 
 }  // namespace
 
+int permute_chunks(int P) { return (P + kChunk - 1) / kChunk; }
+
 // Places caller-supplied pairs into token-major order (validating them) when
 // pairs_in is given; otherwise the router's ids/weights are already token
 // major.  Then counts, scans and scatters.
@@ -328,11 +376,15 @@ cudaError_t launch_permute(const RouterParams& p, const RouteBuffers& rb, const 
   a.tile_break = p.tile_break;
   a.has_shared = p.has_shared;
   a.sort_keys = p.sort_keys;
-  const size_t smem = 3u * p.E * sizeof(uint32_t);
-  permute_count_kernel<<<p.E, kThreads, smem, s>>>(a, rb);
+  const int n_chunks = permute_chunks(P);
+  permute_hist_kernel<<<n_chunks, kThreads, p.E * sizeof(uint32_t), s>>>(a, rb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  permute_scatter_kernel<<<p.E, kThreads, 0, s>>>(a, rb, w16, rb.weights);
+  permute_scan_kernel<<<1, kScanThreads, 3u * p.E * sizeof(uint32_t), s>>>(a, rb, n_chunks);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t smem = (2u + kThreads / 32) * p.E * sizeof(uint32_t);
+  permute_scatter_kernel<<<n_chunks, kThreads, smem, s>>>(a, rb, w16, rb.weights);
   return cudaGetLastError();
 }
 

@@ -190,6 +190,8 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
       take(max_row_tiles(static_cast<uint32_t>(T), static_cast<uint32_t>(K),
                          static_cast<uint32_t>(E), tr) * sizeof(RowTile)));
   rb.n_row_tiles = static_cast<uint32_t*>(take(4));
+  rb.hist = static_cast<uint32_t*>(
+      take(static_cast<size_t>(permute_chunks(static_cast<int>(P))) * E * 4));
   const size_t Td = std::min<size_t>(T, 64);
   rb.xn = static_cast<float*>(take(Td * D * 4));
   rb.xs8 = static_cast<float*>(take(Td * (D / 8) * 4));
@@ -605,7 +607,8 @@ constexpr size_t kGsOffPos = kGsOffW16 + gs_align(kGsPairs * 2);        // u32 [
 constexpr size_t kGsOffTiles = kGsOffPos + gs_align(kGsPairs * 4);      // RowTile [..]
 constexpr size_t kGsOffNTiles = kGsOffTiles + gs_align(kGsRowTiles * sizeof(RowTile));
 constexpr size_t kGsOffCounter = kGsOffNTiles + 256;                    // u32, zero between calls
-constexpr size_t kGsEnd = kGsOffCounter + 256;
+constexpr size_t kGsOffHist = kGsOffCounter + 256;                      // u32 [chunks][512]
+constexpr size_t kGsEnd = kGsOffHist + gs_align((kGsPairs + 2047) / 2048 * 512 * 4);
 static_assert(kGsEnd <= TSG_GROUP_NOALLOC_SCRATCH_BYTES, "group scratch layout overflows");
 
 constexpr int kGsMaxDevices = 64;
@@ -986,6 +989,7 @@ tsg_status tsg_moe_group_pairs_noalloc(tsg_ctx ctx, const tsg_token_expert_pair*
   rb.row_tiles = reinterpret_cast<RowTile*>(base + kGsOffTiles);
   rb.n_row_tiles = reinterpret_cast<uint32_t*>(base + kGsOffNTiles);
   rb.sync_counter = reinterpret_cast<uint32_t*>(base + kGsOffCounter);
+  rb.hist = reinterpret_cast<uint32_t*>(base + kGsOffHist);
   rb.err = ctx->status;
   rb.sorted_pairs = reinterpret_cast<Pair*>(sorted_pairs);
   rb.offsets = offsets;

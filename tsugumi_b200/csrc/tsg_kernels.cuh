@@ -74,6 +74,7 @@ struct RouteBuffers {
   uint32_t* n_row_tiles;  // [1]
   float* xn;              // [T, D] decode only: x * inv_rms in fp32
   float* xs8;             // [T, D/8] decode only: 1.5 x sum of each 8-element run of xn
+  uint32_t* hist;         // [permute_chunks(T*K), E] per-chunk expert counts, then prefixes
   uint32_t* sync_counter; // [1] last-CTA counter, self-resetting
   uint32_t* err;          // [1] device error word
 };
@@ -105,6 +106,8 @@ cudaError_t launch_rowprep(const RouterParams& p, const RouteBuffers& rb, int wr
 cudaError_t launch_group_small(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s);
 int router_prefill_ksplit(int T, int E, int D);
 // permute.cu
+// Chunks of the permutation's counting sort (RouteBuffers::hist rows).
+int permute_chunks(int P);
 cudaError_t launch_permute(const RouterParams& p, const RouteBuffers& rb, const Pair* pairs_in,
                            cudaStream_t s);
 cudaError_t launch_make_pairs(const uint32_t* ids, const uint16_t* w_f16, int T, int K,
