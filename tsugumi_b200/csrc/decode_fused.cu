@@ -838,8 +838,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // rows g: gate f = 8 fb + g (v0, v1), up (v2, v3); columns 2c, 2c+1.
         // Gather the 8 act values of each column to one lane via shuffles.
-        const float a0 = gate_act(p.act, v[0]) * v[2];
-        const float a1 = gate_act(p.act, v[1]) * v[3];
+        const float a0 = gate_act_fast(p.act, v[0]) * v[2];
+        const float a1 = gate_act_fast(p.act, v[1]) * v[3];
         float col[8];
         const int src_c = (lane & 7) >> 1;  // lane n < 8 collects column n
 #pragma unroll
