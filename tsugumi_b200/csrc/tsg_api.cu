@@ -1200,7 +1200,9 @@ tsg_status tsg_shared_expert(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32
   const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
   const uint32_t ntile = (T + tr - 1) / tr;
   RowTile host_tiles[64];
-  if (ntile > 64) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "shared expert call limited to 8192 tokens");
+  if (ntile > 64)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE,
+                "shared expert call limited to " + std::to_string(64u * tr) + " tokens");
   for (uint32_t j = 0; j < ntile; ++j) {
     host_tiles[j].expert = L->desc.num_experts;
     host_tiles[j].row_start = j * tr;

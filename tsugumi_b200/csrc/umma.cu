@@ -14,8 +14,10 @@
 //   * the tensor-core M operand is 128 weight rows (mode 0: 64 gate rows and
 //     the 64 matching up rows, so one accumulator tile holds both halves of
 //     act; mode 1: 128 down rows); the N operand is the row tile of sorted
-//     token rows (<= 128, any multiple of 16), so a lightly routed expert
-//     costs only the rows it has;
+//     token rows (<= 192, any multiple of 16), so a lightly routed expert
+//     costs only the rows it has, and a full tile amortises the issue cost
+//     of each MMA (~100-150 cycles per instruction on one thread) over
+//     N = 192 columns;
 //   * the dequantised weight tile lives in TENSOR MEMORY, not shared memory:
 //     tcgen05.mma reads A from TMEM and only the token tile from shared
 //     memory, which halves the shared-memory traffic per k-step;
@@ -29,9 +31,11 @@
 //     odd k-steps) turn the codes into fp16 and store them into a TMEM ring
 //     of A stages with tcgen05.st; alternating k-steps gives each warp two
 //     k-steps of MMA time to cover the store's completion wait;
-//   * warp 4 moves token tiles with TMA (one 128-row box for a large tile,
-//     16-row boxes for a small one; no multicast);
-//   * warp 6 allocates TMEM (two 128-column fp32 accumulators + the A ring)
+//   * warp 4 moves token tiles with TMA (one 192- or 128-row box for a
+//     large tile, 16-row boxes for a small one; no multicast) into a
+//     three-stage ring;
+//   * warp 6 allocates TMEM (two 192-column fp32 accumulators + a two-stage
+//     A ring of 64 columns each)
 //     and issues tcgen05.mma (M=128, N=rows, K=16), committing to mbarriers;
 //   * warps 0-3 (one per TMEM lane quarter) drain the accumulator with
 //     tcgen05.ld, apply the activation or convert, and store fp16 rows.
@@ -44,7 +48,7 @@
 namespace tsg {
 namespace {
 
-constexpr int kTileN = 128;           // max token rows per tile
+constexpr int kTileN = 192;           // max token rows per tile (MMA N)
 constexpr int kBoxRows = 16;          // small-tile TMA box height (rows)
 constexpr int kKStep = 64;            // K per A/B stage (one 128-byte swizzle row)
 constexpr int kBBytes = kTileN * 128;  // token rows x 64 fp16, 128-byte swizzle
@@ -53,7 +57,8 @@ constexpr int kCodeBytes = 128 * 128;  // 128 weight rows x four k-steps of code
 constexpr int kScaleBoxBytes = 64 * 16;  // mode 0: 64 rows x 8 fp16 scales
 constexpr int kStageK = 2;             // k-steps per A/B stage (one wait + one commit)
 constexpr int kBStageBytes = kStageK * kBBytes;
-constexpr int kMaxStages = 4;          // A (TMEM) / B (smem) ring
+constexpr int kAStages = 2;            // A ring in TMEM (2 x 64 columns after the accumulators)
+constexpr int kMaxBStages = 3;         // B ring in shared memory
 constexpr int kMaxCodeStages = 8;
 constexpr int kThreadsQ = 23 * 32;
 constexpr int kCodeWarp = 5;
@@ -61,12 +66,12 @@ constexpr int kMmaWarp = 6;   // shares its SMSP with epilogue warp 2, which onl
 constexpr int kDqWarp0 = 7;
 constexpr int kNumDqWarps = 16;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCols = 2 * kTileN;  // columns [0, 256): two accumulators
+constexpr uint32_t kAccCols = 2 * kTileN;  // columns [0, 384): two accumulators
 constexpr uint32_t kAKStepCols = kKStep / 2;  // 64 fp16 of K per lane = 32 columns
 constexpr uint32_t kAStageCols = kStageK * kAKStepCols;
 
 struct QMaps {
-  CUtensorMap b16, b128;  // token rows: 16-row and 128-row boxes
+  CUtensorMap b16, b128, b192;  // token rows: 16-, 128- and 192-row boxes
   CUtensorMap w0, w1;     // routed experts' code planes (mode 0: gate, up; 1: down)
   CUtensorMap ws0, ws1;   // the shared expert's
   CUtensorMap sc0, sc1;   // mode 0: routed gate / up scale planes
@@ -92,8 +97,8 @@ struct QArgs {
   int E;
   int act;
   int out_cols;  // F (mode 0) or D (mode 1)
-  int big_box;   // the 128-row token box is usable (>= 128 rows)
-  int stages;    // A/B ring depth
+  int box128, box192;  // the 128- / 192-row token boxes are usable (enough rows)
+  int b_stages;  // B ring depth
   int code_stages;
   uint32_t sc_bytes;  // one scale buffer, 128-byte aligned
   uint32_t c_off, s_off;  // code ring / scale buffers, from the aligned smem base
@@ -102,8 +107,10 @@ struct QArgs {
 };
 
 struct SmemQ {
-  uint64_t full[kMaxStages];  // A stored by the dequantisers + B landed by TMA
-  uint64_t empty[kMaxStages];
+  uint64_t full_a[kAStages];   // A stored by the 16 dequantising warps
+  uint64_t empty_a[kAStages];  // the MMAs that read it are done
+  uint64_t full_b[kMaxBStages];
+  uint64_t empty_b[kMaxBStages];
   uint64_t full_c[kMaxCodeStages];
   uint64_t empty_c[kMaxCodeStages];
   uint64_t full_s[2];
@@ -153,7 +160,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
   __shared__ SmemQ sm;
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - smem_u32(smem_raw));
-  const int S = a.stages, C = a.code_stages;
+  const int SB = a.b_stages, C = a.code_stages;
   constexpr int kCS = CodeStage<MODE>::bytes;
   auto stage_b = [&](int s) { return gbase + s * kBStageBytes; };
   auto stage_c = [&](int c) { return gbase + a.c_off + c * kCS; };
@@ -167,9 +174,13 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
   uint32_t* err = a.err;
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&sm.full[s], kNumDqWarps + 1);
-      mbar_init(&sm.empty[s], 1);
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&sm.full_a[s], kNumDqWarps);
+      mbar_init(&sm.empty_a[s], 1);
+    }
+    for (int s = 0; s < SB; ++s) {
+      mbar_init(&sm.full_b[s], 1);
+      mbar_init(&sm.empty_b[s], 1);
     }
     for (int c = 0; c < C; ++c) {
       mbar_init(&sm.full_c[c], 1);
@@ -200,36 +211,42 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
     // ---------------- TMA producer: token tiles ----------------
     if (lane == 0) {
       prefetch_tensormap(&maps.b16);
-      if (a.big_box) prefetch_tensormap(&maps.b128);
+      if (a.box128) prefetch_tensormap(&maps.b128);
+      if (a.box192) prefetch_tensormap(&maps.b192);
       uint32_t g = 0;
       Ring r;
       bool ok = true;
       for (uint32_t i = 0; i < my_items && ok; ++i) {
         const WorkItem w = work_item(a, n_items, blockIdx.x + i * gridDim.x);
+        // one box for the tile: 192 rows, 128 rows, or 16-row boxes for <= 64
         const uint32_t nbox = (w.rows + kBoxRows - 1) / kBoxRows;
-        const bool big = a.big_box && nbox > 4;
-        const uint32_t step_bytes = big ? static_cast<uint32_t>(kBBytes) : nbox * kBoxRows * 128u;
-        for (int j = 0; j < stages_per_item; ++j, ++g, r.next(S)) {
+        const CUtensorMap* bigmap = (a.box192 && w.rows > 128u) ? &maps.b192
+                                    : (a.box128 && w.rows > 64u) ? &maps.b128
+                                                                 : nullptr;
+        const uint32_t step_bytes = bigmap == &maps.b192 ? 192u * 128u
+                                    : bigmap != nullptr  ? 128u * 128u
+                                                         : nbox * kBoxRows * 128u;
+        for (int j = 0; j < stages_per_item; ++j, ++g, r.next(SB)) {
           const int s = r.s;
-          if (!mbar_sleep(&sm.empty[s], r.ph ^ 1u, err)) { ok = false; break; }
+          if (!mbar_sleep(&sm.empty_b[s], r.ph ^ 1u, err)) { ok = false; break; }
           const int kn = ksteps - kStageK * j < kStageK ? ksteps - kStageK * j : kStageK;
-          mbar_arrive_expect_tx(&sm.full[s], static_cast<uint32_t>(kn) * step_bytes);
+          mbar_arrive_expect_tx(&sm.full_b[s], static_cast<uint32_t>(kn) * step_bytes);
           for (int t = 0; t < kn; ++t) {
             const int ks = kStageK * j + t;
             uint8_t* dst = stage_b(s) + t * kBBytes;
-            if (big) {
-              tma_load_2d(dst, &maps.b128, &sm.full[s], ks * kKStep, static_cast<int32_t>(w.row_start));
+            if (bigmap) {
+              tma_load_2d(dst, bigmap, &sm.full_b[s], ks * kKStep, static_cast<int32_t>(w.row_start));
             } else {
               for (uint32_t b = 0; b < nbox; ++b)
-                tma_load_2d(dst + b * kBoxRows * 128, &maps.b16, &sm.full[s], ks * kKStep,
+                tma_load_2d(dst + b * kBoxRows * 128, &maps.b16, &sm.full_b[s], ks * kKStep,
                             static_cast<int32_t>(w.row_start + b * kBoxRows));
             }
           }
         }
       }
       // drain: the last fill of every stage has landed
-      for (uint32_t q = (g > static_cast<uint32_t>(S) ? g - S : 0); q < g; ++q)
-        mbar_sleep(&sm.full[q % S], (q / S) & 1u, err);
+      for (uint32_t q = (g > static_cast<uint32_t>(SB) ? g - SB : 0); q < g; ++q)
+        mbar_sleep(&sm.full_b[q % SB], (q / SB) & 1u, err);
     }
   } else if (warp == kCodeWarp) {
     // ---------------- TMA producer: code planes and scales ----------------
@@ -288,7 +305,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      Ring r;
+      Ring ra, rb;  // A ring (TMEM), B ring (shared memory)
       bool ok = true;
       for (uint32_t i = 0; i < my_items && ok; ++i) {
         const WorkItem w = work_item(a, n_items, blockIdx.x + i * gridDim.x);
@@ -298,19 +315,19 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
         if (!mbar_sleep(&sm.tmem_empty[acc], ((i >> 1) & 1u) ^ 1u, err)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem + acc * kTileN;
-        for (int j = 0; j < stages_per_item; ++j, r.next(S)) {
-          const int s = r.s;
-          if (!mbar_sleep(&sm.full[s], r.ph, err)) {
+        for (int j = 0; j < stages_per_item; ++j, ra.next(kAStages), rb.next(SB)) {
+          if (!mbar_sleep(&sm.full_a[ra.s], ra.ph, err) || !mbar_sleep(&sm.full_b[rb.s], rb.ph, err)) {
             ok = false;
             break;
           }
           tc_fence_after_sync();
-          const uint32_t a_tmem = tmem + kAccCols + static_cast<uint32_t>(s) * kAStageCols;
-          const uint32_t b0 = smem_u32(stage_b(s));
+          const uint32_t a_tmem = tmem + kAccCols + static_cast<uint32_t>(ra.s) * kAStageCols;
+          const uint32_t b0 = smem_u32(stage_b(rb.s));
           umma_f16_ts_k64(d_tmem, a_tmem, umma_desc_sw128(b0), idesc, j > 0 ? 1u : 0u);
           if (kStageK * j + 1 < ksteps)
             umma_f16_ts_k64(d_tmem, a_tmem + kAKStepCols, umma_desc_sw128(b0 + kBBytes), idesc, 1u);
-          umma_commit(&sm.empty[s]);
+          umma_commit(&sm.empty_a[ra.s]);
+          umma_commit(&sm.empty_b[rb.s]);
         }
         if (ok) umma_commit(&sm.tmem_full[acc]);
       }
@@ -355,7 +372,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
           if (kbase >= ksteps) break;
           const int s = ra.s;
           const uint32_t ph = ra.ph;
-          ra.next(S);
+          ra.next(kAStages);
           const int j = kStageK * jj + par;      // my k-step inside the code stage
           const bool have = k0 + j < ksteps;
           uint32_t o[16];
@@ -386,10 +403,10 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
             tmem_st_wait();
             tc_fence_before_sync();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.full[pend]);
+            if (lane == 0) mbar_arrive(&sm.full_a[pend]);
             pend = -1;
           }
-          if (!warp_wait(&sm.empty[s], ph ^ 1u, err)) { ok = false; break; }
+          if (!warp_wait(&sm.empty_a[s], ph ^ 1u, err)) { ok = false; break; }
           tc_fence_after_sync();
           if (have) tmem_st16(t_row + static_cast<uint32_t>(s) * kAStageCols, o);
           pend = s;
@@ -410,7 +427,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       tmem_st_wait();
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.full[pend]);
+      if (lane == 0) mbar_arrive(&sm.full_a[pend]);
     }
   } else if (warp < 4) {
     // ---------------- epilogue: warps 0-3, TMEM lane quarter = warp ----------------
@@ -543,9 +560,13 @@ cudaError_t launch_qmm(const QmmParams& p, cudaStream_t s) {
   QMaps maps;
   if (!encode_rows(&maps.b16, bsrc, rows, static_cast<uint64_t>(a.K), kBoxRows))
     return cudaErrorInvalidValue;
-  a.big_box = rows >= static_cast<uint64_t>(kTileN) ? 1 : 0;
+  a.box128 = rows >= 128u ? 1 : 0;
+  a.box192 = rows >= 192u ? 1 : 0;
   maps.b128 = maps.b16;
-  if (a.big_box && !encode_rows(&maps.b128, bsrc, rows, static_cast<uint64_t>(a.K), kTileN))
+  maps.b192 = maps.b16;
+  if (a.box128 && !encode_rows(&maps.b128, bsrc, rows, static_cast<uint64_t>(a.K), 128u))
+    return cudaErrorInvalidValue;
+  if (a.box192 && !encode_rows(&maps.b192, bsrc, rows, static_cast<uint64_t>(a.K), 192u))
     return cudaErrorInvalidValue;
   // code planes (and, for mode 0, scale planes) of the routed and shared experts
   const uint64_t row_bytes = static_cast<uint64_t>(a.K) / 2;
@@ -599,17 +620,17 @@ cudaError_t launch_qmm(const QmmParams& p, cudaStream_t s) {
   if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kern);
   if (e != cudaSuccess) return e;
   a.sc_bytes = MODE == 1 ? (128u * static_cast<uint32_t>(a.K) / 16u + 127u) & ~127u : 0u;
-  int S = kMaxStages, C = kMaxCodeStages;
+  int S = kMaxBStages, C = kMaxCodeStages;
   auto need = [&]() {
     return static_cast<size_t>(1024) + static_cast<size_t>(S) * kBStageBytes +
            static_cast<size_t>(C) * CodeStage<MODE>::bytes + 2u * static_cast<size_t>(a.sc_bytes);
   };
   while (need() + fa.sharedSizeBytes > static_cast<size_t>(optin)) {
-    if (C > 4) --C;
+    if (C > 3) --C;
     else if (S > 2) --S;
     else return cudaErrorInvalidValue;
   }
-  a.stages = S;
+  a.b_stages = S;
   a.code_stages = C;
   a.c_off = static_cast<uint32_t>(S * kBStageBytes);
   a.s_off = a.c_off + static_cast<uint32_t>(C * CodeStage<MODE>::bytes);
