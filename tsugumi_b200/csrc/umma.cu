@@ -10,7 +10,7 @@
 // per-route partials.  Weights are dequantised once to fp16 and multiplied
 // with fp32 accumulation.
 //
-// B200 design (one persistent CTA per SM, warp-specialised, 23 warps):
+// B200 design (one persistent CTA per SM, warp-specialised, 27 warps):
 //   * the tensor-core M operand is 128 weight rows (mode 0: 64 gate rows and
 //     the 64 matching up rows, so one accumulator tile holds both halves of
 //     act; mode 1: 128 down rows); the N operand is the row tile of sorted
@@ -37,8 +37,9 @@
 //   * warp 6 allocates TMEM (two 192-column fp32 accumulators + a two-stage
 //     A ring of 64 columns each)
 //     and issues tcgen05.mma (M=128, N=rows, K=16), committing to mbarriers;
-//   * warps 0-3 (one per TMEM lane quarter) drain the accumulator with
-//     tcgen05.ld, apply the activation or convert, and store fp16 rows.
+//   * warps 0-3 and 23-26 (two per TMEM lane quarter, alternate 16-column
+//     chunks) drain the accumulator with tcgen05.ld, apply the activation
+//     or convert, and store fp16 rows.
 // Every wait is bounded (tsg_common.cuh) and every wait that guards a
 // warp-collective tcgen05 instruction is made warp-uniform, so a fault in
 // the pipeline ends the kernel with an error flag instead of hanging.
@@ -60,7 +61,9 @@ constexpr int kBStageBytes = kStageK * kBBytes;
 constexpr int kAStages = 2;            // A ring in TMEM (2 x 64 columns after the accumulators)
 constexpr int kMaxBStages = 3;         // B ring in shared memory
 constexpr int kMaxCodeStages = 8;
-constexpr int kThreadsQ = 23 * 32;
+constexpr int kThreadsQ = 27 * 32;
+constexpr int kEpiWarp1 = 23;          // warps 0-3 and 23-26 drain the accumulators
+constexpr int kEpiWarps = 8;
 constexpr int kCodeWarp = 5;
 constexpr int kMmaWarp = 6;   // shares its SMSP with epilogue warp 2, which only hands values over
 constexpr int kDqWarp0 = 7;
@@ -190,7 +193,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       mbar_init(&sm.full_s[i], 1);
       mbar_init(&sm.empty_s[i], kNumDqWarps);
       mbar_init(&sm.tmem_full[i], 1);
-      mbar_init(&sm.tmem_empty[i], 4);
+      mbar_init(&sm.tmem_empty[i], kEpiWarps);
     }
     fence_mbar_init();
   }
@@ -315,8 +318,10 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
         if (!mbar_sleep(&sm.tmem_empty[acc], ((i >> 1) & 1u) ^ 1u, err)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem + acc * kTileN;
+        bool ready = false;  // the next stage's A and B were seen ready already
         for (int j = 0; j < stages_per_item; ++j, ra.next(kAStages), rb.next(SB)) {
-          if (!mbar_sleep(&sm.full_a[ra.s], ra.ph, err) || !mbar_sleep(&sm.full_b[rb.s], rb.ph, err)) {
+          if (!ready &&
+              (!mbar_sleep(&sm.full_a[ra.s], ra.ph, err) || !mbar_sleep(&sm.full_b[rb.s], rb.ph, err))) {
             ok = false;
             break;
           }
@@ -326,13 +331,20 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
           umma_f16_ts_k64(d_tmem, a_tmem, umma_desc_sw128(b0), idesc, j > 0 ? 1u : 0u);
           if (kStageK * j + 1 < ksteps)
             umma_f16_ts_k64(d_tmem, a_tmem + kAKStepCols, umma_desc_sw128(b0 + kBBytes), idesc, 1u);
+          // look at the next stage's barriers before the commits, so that
+          // the answer is back by the time the loop needs it
+          Ring na = ra, nb = rb;
+          na.next(kAStages);
+          nb.next(SB);
+          ready = j + 1 < stages_per_item && mbar_try_wait(&sm.full_a[na.s], na.ph) &&
+                  mbar_try_wait(&sm.full_b[nb.s], nb.ph);
           umma_commit(&sm.empty_a[ra.s]);
           umma_commit(&sm.empty_b[rb.s]);
         }
         if (ok) umma_commit(&sm.tmem_full[acc]);
       }
     }
-  } else if (warp >= kDqWarp0) {
+  } else if (warp >= kDqWarp0 && warp < kDqWarp0 + kNumDqWarps) {
     // ---------------- dequantisers: codes -> fp16 A tile in TMEM ----------------
     // Warp w serves TMEM lanes 32*(w%4).. (its hardware lane quarter); role
     // r = (w - 7) / 4 picks half h = r & 1 of a k-step and which k-step
@@ -429,11 +441,13 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.full_a[pend]);
     }
-  } else if (warp < 4) {
-    // ---------------- epilogue: warps 0-3, TMEM lane quarter = warp ----------------
-    // A failed wait does not leave the loop: the warp only skips the TMEM
-    // reads and the stores.
-    const int q = warp;  // lanes 32q .. 32q+31
+  } else if (warp < 4 || warp >= kEpiWarp1) {
+    // ---------------- epilogue: warps 0-3 and 23-26 ----------------
+    // Two warps per TMEM lane quarter (q = warp % 4), taking alternate
+    // 16-column chunks.  A failed wait does not leave the loop: the warp
+    // only skips the TMEM reads and the stores.
+    const int q = warp & 3;  // lanes 32q .. 32q+31
+    const uint32_t c_first = warp < 4 ? 0u : 16u;
     const bool upper = lane >= 16;
     for (uint32_t i = 0; i < my_items; ++i) {
       const WorkItem w = work_item(a, n_items, blockIdx.x + i * gridDim.x);
@@ -442,7 +456,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       tc_fence_after_sync();
       const uint32_t n = (w.rows + 15u) & ~15u;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(32 * q) << 16) + acc * kTileN;
-      for (uint32_t c0 = 0; ok && c0 < n; c0 += 16) {
+      for (uint32_t c0 = c_first; ok && c0 < n; c0 += 32) {
         uint32_t r[16];
         tmem_ld16(tbase + c0, r);
         tmem_ld_wait();
