@@ -135,7 +135,7 @@ def build_stack(ctx, n_layers: int, skew, device, seed0: int):
     return layers
 
 
-def distinct_experts(ctx, layers, x0, T):
+def distinct_experts(ctx, layers, x0, T, k=K):
     """Runs the stack once un-captured and counts the distinct experts each
     layer reads (u(T), the unit of the decode roofline)."""
     import torch
@@ -144,8 +144,8 @@ def distinct_experts(ctx, layers, x0, T):
     us = []
     x = x0
     for lay in layers:
-        ids = torch.empty((T, K), dtype=torch.int32, device=x.device)
-        w = torch.empty((T, K), dtype=torch.float32, device=x.device)
+        ids = torch.empty((T, k), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, k), dtype=torch.float32, device=x.device)
         tb.MoE(ctx, lay).encode_router_gemma4_bf16(x, ids, w)
         y = lay.forward(x)
         ctx.sync()
@@ -157,8 +157,8 @@ def distinct_experts(ctx, layers, x0, T):
 def capture_stack(ctx, layers, x_in, profile: bool):
     import torch
 
-    T = x_in.shape[0]
-    bufs = [torch.empty((T, D), dtype=torch.bfloat16, device=x_in.device) for _ in range(2)]
+    T, d = x_in.shape
+    bufs = [torch.empty((T, d), dtype=torch.bfloat16, device=x_in.device) for _ in range(2)]
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
@@ -318,6 +318,10 @@ def run_ours(args):
             sweep.update(run_decode_sweep(ctx, layers, device, args, barrier))
         except Exception as exc:
             sweep["decode_sweep_error"] = repr(exc)
+        try:
+            sweep.update(run_qwen_sweep(ctx, device, args, barrier))
+        except Exception as exc:
+            sweep["qwen_sweep_error"] = repr(exc)
         sweep.update(run_ep_sweep(device, args, rank, world, local))
 
     result = {
@@ -393,6 +397,70 @@ def run_decode_sweep(ctx, layers, device, args, barrier):
         out[f"decode_T{T}"] = {"layer_tokens_per_s": T * LAYERS / (ms / 1e3), "ms_per_step": ms,
                                "u_mean": float(np.mean(us)), "expert_gbs": gbs,
                                "hbm_frac": gbs / pk["hbm_gbs"]}
+    return out
+
+
+def run_qwen_sweep(ctx, device, args, barrier):
+    """the Qwen-like layer (256 experts, top-8, SwiGLU, a shared
+    expert of FFN 512 behind a sigmoid gate) on a 40-layer stack: decode at
+    T = 1 and 64 (CUDA graphs of the stack) and prefill at T = 4096 (4 of the
+    layers, unskewed routing).  Decode bytes per layer: u(T) routed experts +
+    the shared expert, codes and scales."""
+    import torch
+    import tsugumi_b200 as tb
+    from tsugumi_b200.synthetic import CONFIGS, device_layer_tensors
+
+    qd, qf, qe, qk, _, qsf = CONFIGS["qwen"]
+    ebytes = 3 * (qf * qd // 2 + qf * (qd // 32) * 2)
+    sbytes = 3 * (qsf * qd // 2 + qsf * (qd // 32) * 2)
+    n_layers = 40
+    pk = peaks()
+    steps = max(3, args.steps // 4)
+    layers = [tb.MoELayer(ctx, device_layer_tensors("qwen", 3 + 7919 * l, None, device))
+              for l in range(n_layers)]
+    ctx.reserve(layers[0], 64)
+    out = {}
+    for T in (1, 64):
+        gen = torch.Generator(device=device)
+        gen.manual_seed(3000 + T)
+        x0 = torch.randn((T, qd), generator=gen, device=device).to(torch.bfloat16)
+        us = distinct_experts(ctx, layers, x0, T, k=qk)
+        g, _ = capture_stack(ctx, layers, x0, profile=False)
+        ms = timed_replays(g, steps, 3, barrier)
+        del g
+        bytes_ = (float(np.mean(us)) * ebytes + sbytes) * n_layers
+        gbs = bytes_ / (ms / 1e3) / 1e9
+        out[f"qwen_decode_T{T}"] = {"layer_tokens_per_s": T * n_layers / (ms / 1e3),
+                                    "ms_per_step": ms, "layers": n_layers,
+                                    "u_mean": float(np.mean(us)), "expert_gbs": gbs,
+                                    "hbm_frac": gbs / pk["hbm_gbs"]}
+    T = 4096
+    pre = layers[:4]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4097)
+    x0 = torch.randn((T, qd), generator=gen, device=device).to(torch.bfloat16)
+    ctx.reserve(pre[0], T)
+    y = torch.empty((T, qd), dtype=torch.bfloat16, device=device)
+    for _ in range(2):
+        for lay in pre:
+            lay.forward(x0, y=y)
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        for lay in pre:
+            lay.forward(x0, y=y)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_layer = e0.elapsed_time(e1) / (steps * len(pre))
+    flops = 2.0 * T * (qk * 3 * qd * qf + 3 * qd * qsf)
+    out["qwen_prefill_T4096"] = {"layer_tokens_per_s": T / (ms_layer / 1e3), "ms_per_layer": ms_layer,
+                                 "tflops": flops / (ms_layer / 1e3) / 1e12,
+                                 "tensor_frac": flops / (ms_layer / 1e3) / 1e12 / pk["bf16_tflops"]}
+    for lay in layers:
+        lay.close()
+    del layers
+    torch.cuda.empty_cache()
     return out
 
 
