@@ -268,12 +268,22 @@ def test_decode_and_prefill_regimes_agree(ctx, name, T):
     assert rel_l2(y_pre.cpu().numpy(), y_dec.cpu().numpy()) < REL_L2
 
 
-@pytest.mark.parametrize("which,T", [("decode", 3), ("decode", 8), ("prefill", 200)])
-def test_experts_with_caller_routing(ctx, which, T):
+@pytest.mark.parametrize("which,T,hot", [
+    ("decode", 3, False), ("decode", 8, False), ("prefill", 200, False),
+    # caller routing may send every slot of every token to one expert: one
+    # row tile of T*K rows with no more rows in the whole buffer (160: larger
+    # than a 128-row token box, smaller than the 192-row one), exactly one
+    # full tile (192), and a full tile plus a ragged one (240)
+    ("prefill", 20, True), ("prefill", 24, True), ("prefill", 30, True)])
+def test_experts_with_caller_routing(ctx, which, T, hot):
     host, dev, ol = layer_pair(ctx, "gemma", 11, None)
     x = host_tokens(T, host.d, 55)
     rng = np.random.default_rng(5)
-    ids = np.stack([rng.choice(host.num_experts, host.top_k, replace=False) for _ in range(T)])
+    if hot:
+        ids = np.full((T, host.top_k), 7, dtype=np.int64)
+    else:
+        ids = np.stack([rng.choice(host.num_experts, host.top_k, replace=False)
+                        for _ in range(T)])
     w = rng.uniform(0.05, 0.3, (T, host.top_k)).astype(np.float32)
     resid = rng.standard_normal((T, host.d)).astype(np.float32)
     y = torch.empty((T, host.d), dtype=torch.float32, device="cuda")

@@ -221,14 +221,17 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       bool ok = true;
       for (uint32_t i = 0; i < my_items && ok; ++i) {
         const WorkItem w = work_item(a, n_items, blockIdx.x + i * gridDim.x);
-        // one box for the tile: 192 rows, 128 rows, or 16-row boxes for <= 64
+        // one box for the tile when a box that covers it exists (192 rows
+        // for a tile of 129-192, 128 rows for 65-128; a box map exists only
+        // when the buffer has that many rows), else 16-row boxes
         const uint32_t nbox = (w.rows + kBoxRows - 1) / kBoxRows;
-        const CUtensorMap* bigmap = (a.box192 && w.rows > 128u) ? &maps.b192
-                                    : (a.box128 && w.rows > 64u) ? &maps.b128
-                                                                 : nullptr;
-        const uint32_t step_bytes = bigmap == &maps.b192 ? 192u * 128u
-                                    : bigmap != nullptr  ? 128u * 128u
-                                                         : nbox * kBoxRows * 128u;
+        const CUtensorMap* bigmap = nullptr;
+        uint32_t step_bytes = nbox * kBoxRows * 128u;
+        if (w.rows > 128u) {
+          if (a.box192) { bigmap = &maps.b192; step_bytes = 192u * 128u; }
+        } else if (w.rows > 64u) {
+          if (a.box128) { bigmap = &maps.b128; step_bytes = 128u * 128u; }
+        }
         for (int j = 0; j < stages_per_item; ++j, ++g, r.next(SB)) {
           const int s = r.s;
           if (!mbar_sleep(&sm.empty_b[s], r.ph ^ 1u, err)) { ok = false; break; }
