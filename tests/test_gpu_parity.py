@@ -89,6 +89,11 @@ ROUTER_CASES = [
     ("qwen", 16, None, 64),
     ("qwen", 300, None, 64),
     ("tiny", 40, None, 0),  # prefill router kernels on a small batch
+    # tensor-core prefill router: a partial second token tile, 16 experts in
+    # a zero-padded 128-row tile, a large batch
+    ("gemma", 200, None, 0),
+    ("tiny", 300, None, 0),
+    ("qwen", 4096, None, 0),
 ]
 
 

@@ -444,14 +444,25 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(RouterParams p, RouteB
 }
 
 // Warp per token: combine the splits, apply the norm factor and bias, select.
+// With ss_from_x the row's sum of squares is taken from its bf16 input (the
+// tensor-core GEMM produces only the dots), else from the split partials.
 __global__ void __launch_bounds__(256) router_topk_kernel(RouterParams p, RouteBuffers rb,
-                                                          int ksplit) {
+                                                          int ksplit, int ss_from_x) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= p.T) return;
   const int t = warp;
   float ssq = 0.0f;
-  for (int s = 0; s < ksplit; ++s) ssq += rb.sumsq[static_cast<size_t>(s) * p.T + t];
+  if (ss_from_x) {
+    const uint16_t* xr = p.x + static_cast<size_t>(t) * p.x_stride;
+    for (int i = lane; i < p.D; i += 32) {
+      const float v = bf16_bits_to_f32(xr[i]);
+      ssq = fmaf(v, v, ssq);
+    }
+    ssq = warp_sum(ssq);
+  } else {
+    for (int s = 0; s < ksplit; ++s) ssq += rb.sumsq[static_cast<size_t>(s) * p.T + t];
+  }
   const float inv = p.norm ? rsqrtf(ssq / static_cast<float>(p.D) + p.eps) : 1.0f;
   if (lane == 0) rb.inv_rms[t] = inv;
   dispatch_token_topk(rb.logits_raw + static_cast<size_t>(t) * p.E, ksplit,
@@ -536,13 +547,22 @@ cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb,
   const int mt = (p.T + kGBM - 1) / kGBM;
   const int nt = (p.E + kGBN - 1) / kGBN;
   int ksplit = 1;
-  while (mt * nt * ksplit < 148 && ksplit < 8 && p.D / (ksplit * 2) >= 256) ksplit *= 2;
-  dim3 grid(mt, nt, ksplit);
-  router_gemm_kernel<<<grid, 256, 0, s>>>(p, rb, ksplit);
-  cudaError_t e = cudaGetLastError();
+  int from_x = 0;
+  cudaError_t e;
+  if (router_tc_usable(p)) {
+    ksplit = router_tc_ksplit(p.T, p.E, p.D);
+    from_x = 1;
+    e = launch_router_tc(p, rb, ksplit, s);
+  } else {
+    while (mt * nt * ksplit < 148 && ksplit < 8 && p.D / (ksplit * 2) >= 256) ksplit *= 2;
+    dim3 grid(mt, nt, ksplit);
+    router_gemm_kernel<<<grid, 256, 0, s>>>(p, rb, ksplit);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return e;
   const int warps_per_cta = 8;
-  router_topk_kernel<<<(p.T + warps_per_cta - 1) / warps_per_cta, 256, 0, s>>>(p, rb, ksplit);
+  router_topk_kernel<<<(p.T + warps_per_cta - 1) / warps_per_cta, 256, 0, s>>>(p, rb, ksplit,
+                                                                              from_x);
   return cudaGetLastError();
 }
 

@@ -100,6 +100,7 @@ struct tsg_moe_layer_s {
   tsg_ctx ctx = nullptr;
   tsg_moe_layer_desc desc{};
   float* router_rows = nullptr;  // [E + has_gate][D], owned
+  void* router_w3 = nullptr;     // [3][router_tc_pad(E)][D] bf16 planes of the first E rows, owned
   int has_gate = 0;
   int has_shared = 0;
 };
@@ -261,6 +262,7 @@ RouterParams router_params(const tsg_moe_layer_s* L, const void* x, uint32_t x_s
   p.E = static_cast<int>(L->desc.num_experts);
   p.K = static_cast<int>(L->desc.top_k);
   p.w = L->router_rows;
+  p.w_bf16x3 = L->router_w3;
   p.has_gate = L->has_gate;
   p.has_shared = L->has_shared;
   p.per_expert_scale = L->desc.per_expert_scale;
@@ -771,8 +773,17 @@ tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc* d, tsg_mo
                                                      static_cast<int>(d->d), L->router_rows);
     e = cudaGetLastError();
   }
+  if (e == cudaSuccess && d->d % 64 == 0) {
+    // exact bf16 planes for the tensor-core prefill router
+    const size_t bytes = 3ull * router_tc_pad(static_cast<int>(d->num_experts)) * d->d * 2;
+    e = cudaMalloc(&L->router_w3, bytes);
+    if (e == cudaSuccess)
+      e = launch_split_router(L->router_rows, static_cast<int>(d->num_experts),
+                              static_cast<int>(d->d), L->router_w3, ctx->stream);
+  }
   if (e != cudaSuccess) {
     if (L->router_rows) cudaFree(L->router_rows);
+    if (L->router_w3) cudaFree(L->router_w3);
     delete L;
     return cuda_fail(ctx, e, "layer create");
   }
@@ -785,6 +796,7 @@ tsg_status tsg_moe_layer_destroy(tsg_moe_layer L) {
   // the layer does not touch its context here: contexts and layers may be
   // destroyed in either order (cudaFree waits for outstanding work itself)
   if (L->router_rows) cudaFree(L->router_rows);
+  if (L->router_w3) cudaFree(L->router_w3);
   delete L;
   return TSG_OK;
 }

@@ -84,6 +84,7 @@ struct RouterParams {
   uint32_t x_stride;
   int T, D, E, K;
   const float* w;          // [E + has_gate, D] router rows (effective scale folded in)
+  const void* w_bf16x3;    // [3][router_tc_pad(E)][D] bf16 hi/mid/lo planes of w, or nullptr
   int has_gate;            // 1: row E is the shared-expert gate vector
   int has_shared;          // 1: the layer has a shared expert
   const float* per_expert_scale;  // [E] or nullptr
@@ -105,6 +106,15 @@ cudaError_t launch_rowprep(const RouterParams& p, const RouteBuffers& rb, int wr
                            cudaStream_t s);
 cudaError_t launch_group_small(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s);
 int router_prefill_ksplit(int T, int E, int D);
+
+// router_tc.cu: the prefill router GEMM on tcgen05 (exact fp32 through three
+// bf16 planes of the router rows, made once per layer)
+int router_tc_pad(int E);
+cudaError_t launch_split_router(const float* w, int E, int D, void* planes, cudaStream_t s);
+bool router_tc_usable(const RouterParams& p);
+int router_tc_ksplit(int T, int E, int D);
+cudaError_t launch_router_tc(const RouterParams& p, const RouteBuffers& rb, int ksplit,
+                             cudaStream_t s);
 // permute.cu
 // Chunks of the permutation's counting sort (RouteBuffers::hist rows).
 int permute_chunks(int P);
