@@ -51,19 +51,22 @@ def layer_pair(ctx, name, seed, skew=None):
 
 
 class regime:
-    """Temporarily selects the regime: decode_max_tokens and the fused
-    single-kernel decode switch."""
+    """Temporarily selects the regime: decode_max_tokens, the fused
+    single-kernel decode switch and the largest batch the batched GEMVs
+    take (0: small batches use the tensor-core contraction too)."""
 
-    def __init__(self, ctx, dmax=4, fused=True):
-        self.ctx, self.dmax, self.fused = ctx, dmax, fused
+    def __init__(self, ctx, dmax=4, fused=True, gemv=64):
+        self.ctx, self.dmax, self.fused, self.gemv = ctx, dmax, fused, gemv
 
     def __enter__(self):
         self.ctx.set_decode_max_tokens(self.dmax)
         self.ctx.set_option("fused_decode", 1 if self.fused else 0)
+        self.ctx.set_option("gemv_max_tokens", self.gemv)
 
     def __exit__(self, *exc):
         self.ctx.set_decode_max_tokens(4)
         self.ctx.set_option("fused_decode", 1)
+        self.ctx.set_option("gemv_max_tokens", 16)
 
 
 def gpu_route(ctx, layer, x_dev):
@@ -89,6 +92,10 @@ ROUTER_CASES = [
     ("qwen", 16, None, 64),
     ("qwen", 300, None, 64),
     ("tiny", 40, None, 0),  # prefill router kernels on a small batch
+    # small-batch prefill router (T <= 64): ragged token passes, split D
+    ("gemma", 8, None, 0),
+    ("gemma", 64, 1.1, 0),
+    ("qwen", 33, None, 0),
     # tensor-core prefill router: a partial second token tile, 16 experts in
     # a zero-padded 128-row tile, a large batch
     ("gemma", 200, None, 0),
@@ -207,6 +214,12 @@ BLOCK_CASES = [
     ("gemma", 4096, 1.1, 4, True, 48),
     ("qwen", 1024, None, 4, True, 48),
     ("gemma", 48, None, 0, True, None),
+    # 4 < T <= 64: batched GEMVs (ragged token blocks, few rows per expert)
+    ("tiny", 5, None, 4, True, None),
+    ("gemma", 9, None, 4, True, None),
+    ("gemma", 64, 1.1, 4, True, None),
+    ("qwen", 33, None, 4, True, None),
+    ("qwen", 64, None, 4, True, None),
 ]
 
 
@@ -259,6 +272,23 @@ def test_fused_decode_graph_replay_is_stable(ctx, name, T):
         assert torch.equal(y, y0)
     ctx.sync()
     del g
+
+
+@pytest.mark.parametrize("name,T", [("tiny", 7), ("gemma", 24), ("qwen", 64)])
+def test_small_batch_gemv_matches_contraction(ctx, name, T):
+    """The batched GEMVs and the tensor-core contraction compute the same
+    expert products for a small router-driven batch."""
+    host, dev, ol = layer_pair(ctx, name, 11, None)
+    xd = to_dev(host_tokens(T, host.d, 5 + T))
+    with regime(ctx, 4, True, 64):
+        y_gemv = dev.forward(xd, out_dtype=torch.float32)
+        ctx.sync()
+    with regime(ctx, 4, True, 0):
+        y_qmm = dev.forward(xd, out_dtype=torch.float32)
+        ctx.sync()
+    err = rel_l2(y_gemv.cpu().numpy(), y_qmm.cpu().numpy())
+    print(f"{name} T={T}: gemv vs contraction rel L2 {err:.3e}")
+    assert err < REL_L2
 
 
 @pytest.mark.parametrize("name,T", [("gemma", 4), ("qwen", 32)])

@@ -59,6 +59,7 @@
 
 #include "tsg_common.cuh"
 #include "tsg_kernels.cuh"
+#include "int4_mma.cuh"
 
 namespace tsg {
 namespace {
@@ -183,37 +184,9 @@ __host__ __device__ inline uint32_t plan_rings(uint32_t su, uint32_t sd, uint32_
   return region;
 }
 
-TSG_DEV void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                       uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 
-// (a & b) | c in one instruction.
-TSG_DEV uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-  return r;
-}
 
-TSG_DEV uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-TSG_DEV __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// A code word as four scaled fp16 pairs s (q - 8):
-// p[0] = (e0,e4), p[1] = (e2,e6), p[2] = (e1,e5), p[3] = (e3,e7).
-// s2 = (s, s), s16 = (s / 16, s / 16).
-TSG_DEV void dequant_word(uint32_t w, __half2 s2, __half2 s16, uint32_t (&p)[4]) {
-  const uint32_t w8 = w >> 8;
-  const __half2 lo_off = __floats2half2_rn(1032.0f, 1032.0f);
-  const __half2 hi_off = __floats2half2_rn(1152.0f, 1152.0f);
-  p[0] = h2_bits(__hmul2(__hsub2(bits_h2(and_or(w, 0x000F000Fu, 0x64006400u)), lo_off), s2));
-  p[1] = h2_bits(__hmul2(__hsub2(bits_h2(and_or(w8, 0x000F000Fu, 0x64006400u)), lo_off), s2));
-  p[2] = h2_bits(__hmul2(__hsub2(bits_h2(and_or(w, 0x00F000F0u, 0x64006400u)), hi_off), s16));
-  p[3] = h2_bits(__hmul2(__hsub2(bits_h2(and_or(w8, 0x00F000F0u, 0x64006400u)), hi_off), s16));
-}
 
 // Eight consecutive activations as the matching B fragment chunk
 // [(v0,v4), (v2,v6), (v1,v5), (v3,v7)] in fp16.
@@ -239,12 +212,6 @@ TSG_DEV void mma_supergroup(float (&acc)[4], const uint4& ra, const uint4& rb, _
   }
 }
 
-TSG_DEV void scale_pair(const __half* s, __half2* s2, __half2* s16) {
-  const __half h = *s;
-  *s2 = __halves2half2(h, h);
-  const __half q = __hmul(h, __float2half_rn(0.0625f));
-  *s16 = __halves2half2(q, q);
-}
 
 // a / b for small non-negative ints (a < 2^16, b <= 4096) through a float
 // reciprocal of b: a few instructions instead of an integer division.

@@ -19,6 +19,7 @@
 //      per-warp counts, so the order inside an expert is (token, rank).
 // Output is bit-identical to the reference's sort by (key, expert, token,
 // rank).
+#include "int4_mma.cuh"
 #include "tsg_common.cuh"
 #include "tsg_kernels.cuh"
 
@@ -301,12 +302,14 @@ __global__ void make_pairs_kernel(const uint32_t* ids, const uint16_t* w16, int 
 // Row i < n_rows takes token sorted_pairs[i].token; rows n_rows + t (when
 // append_tokens) take token t in order (the shared expert's input).  One warp
 // per row; also computes the raw shared-gate dot for the appended rows.
+// With `frag_order` each 8 elements are stored as x0 x4 x2 x6 x1 x5 x3 x7,
+// the mma.sync operand order of the batched GEMVs (int4_mma.cuh).
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, uint32_t x_stride,
                                                           const float* inv_rms,
                                                           const Pair* sorted_pairs, int n_rows,
                                                           int T, int D, int append_tokens,
                                                           __half* xp, const float* gate_w,
-                                                          float* gate_raw) {
+                                                          float* gate_raw, int frag_order) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int total = n_rows + (append_tokens ? T : 0);
@@ -333,7 +336,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, uin
       __half2 h = __floats2half2_rn(a * inv, b * inv);
       o[j] = *reinterpret_cast<uint32_t*>(&h);
     }
-    dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    const uint4 v8 = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[c] = frag_order ? frag_from_row(v8) : v8;
   }
   if (do_gate) {
     g = warp_sum(g);
@@ -399,12 +403,13 @@ cudaError_t launch_make_pairs(const uint32_t* ids, const uint16_t* w_f16, int T,
 cudaError_t launch_gather_rows_gate(const uint16_t* x, uint32_t x_stride, const float* inv_rms,
                                     const Pair* sorted_pairs, int n_rows, int T, int D,
                                     int append_tokens, __half* xp, const float* gate_w,
-                                    float* gate_raw, cudaStream_t s) {
+                                    float* gate_raw, cudaStream_t s, int frag_order) {
   const int total = n_rows + (append_tokens ? T : 0);
   if (total <= 0) return cudaSuccess;
   const int warps_per_cta = 8;
   gather_rows_kernel<<<(total + warps_per_cta - 1) / warps_per_cta, 256, 0, s>>>(
-      x, x_stride, inv_rms, sorted_pairs, n_rows, T, D, append_tokens, xp, gate_w, gate_raw);
+      x, x_stride, inv_rms, sorted_pairs, n_rows, T, D, append_tokens, xp, gate_w, gate_raw,
+      frag_order);
   return cudaGetLastError();
 }
 

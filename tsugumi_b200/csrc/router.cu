@@ -21,6 +21,7 @@ namespace {
 constexpr int kDecodeRowsPerCta = 8;  // one warp per router row
 constexpr int kDecodeTokChunk = 8;    // tokens staged per pass
 constexpr int kMaxK = 32;
+constexpr int kMaxSplitParts = 8;  // split-K partials of the prefill router GEMMs
 
 // Select the top K of `v` (lane holds v[lane + 32 j], j < per_lane) with the
 // reference's tie rule.  Lane 0 ends with ids[0..K) and scores[0..K).
@@ -90,7 +91,12 @@ __device__ void token_topk(const float* raw, int nsplit, size_t split_stride, fl
     const int e = lane + 32 * j;
     float s = 0.0f;
     if (e < p.E) {
-      for (int sp = 0; sp < nsplit; ++sp) s += __ldcg(raw + sp * split_stride + e);
+      float part[kMaxSplitParts];
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplitParts; ++sp)  // loads issued together
+        part[sp] = sp < nsplit ? __ldcg(raw + sp * split_stride + e) : 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplitParts; ++sp) s += part[sp];
       s *= inv;
       if (p.logit_bias) s += p.logit_bias[e];
     } else {
@@ -443,6 +449,108 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(RouterParams p, RouteB
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill router for small batches (T <= 64): one warp per router row and
+// split of D (chunks of 256 columns, 8 per lane); tokens in passes of 16
+// accumulated in registers, then reduced across lanes by halving exchanges
+// (16 values to one per lane pair in 16 shuffles).  The weight rows stream
+// once from HBM; the token rows come from L1.  CTA column 0, warp 0 also
+// writes the split's row sums of squares.  Same outputs as router_gemm.
+// ---------------------------------------------------------------------------
+constexpr int kSmallRows = 4;     // router rows (warps) per CTA
+constexpr int kSmallChunk = 256;  // columns per lane pass (8 per lane)
+constexpr int kSmallPass = 16;    // tokens per pass
+
+// v[16] per lane -> lanes 2j and 2j + 1 hold the warp-wide sum of v[j].
+TSG_DEV float reduce16(float (&v)[kSmallPass]) {
+  const int lane = threadIdx.x & 31;
+  float u[8];
+  const bool b4 = lane & 16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float send = b4 ? v[i] : v[i + 8];
+    const float keep = b4 ? v[i + 8] : v[i];
+    u[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+  }
+  const bool b3 = lane & 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b3 ? u[i] : u[i + 4];
+    const float keep = b3 ? u[i + 4] : u[i];
+    u[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 8);
+  }
+  const bool b2 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b2 ? u[i] : u[i + 2];
+    const float keep = b2 ? u[i + 2] : u[i];
+    u[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 4);
+  }
+  const bool b1 = lane & 2;
+  {
+    const float send = b1 ? u[0] : u[1];
+    const float keep = b1 ? u[1] : u[0];
+    u[0] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, 2);
+  }
+  return u[0] + __shfl_xor_sync(0xFFFFFFFFu, u[0], 1);
+}
+
+__global__ void __launch_bounds__(kSmallRows * 32) router_small_kernel(RouterParams p,
+                                                                        RouteBuffers rb,
+                                                                        int chunks_per_split) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = blockIdx.x * kSmallRows + warp;
+  const int split = blockIdx.y;
+  const int k0 = split * chunks_per_split * kSmallChunk;
+  const int k1 = min(p.D, k0 + chunks_per_split * kSmallChunk);
+  const bool row_ok = e < p.E;
+  const bool ss_warp = blockIdx.x == 0 && warp == 0;
+  const float* wr = p.w + static_cast<size_t>(row_ok ? e : 0) * p.D;
+  const int j = lane >> 1;  // the token slot this lane pair ends with
+  for (int t0 = 0; t0 < p.T; t0 += kSmallPass) {
+    float acc[kSmallPass], ss[kSmallPass];
+#pragma unroll
+    for (int t = 0; t < kSmallPass; ++t) acc[t] = ss[t] = 0.0f;
+    for (int k = k0 + lane * 8; k < k1; k += kSmallChunk) {
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(wr + k));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(wr + k + 4));
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      // every token load of the pass in flight before the first FMA
+      uint4 xv[kSmallPass];
+#pragma unroll
+      for (int t = 0; t < kSmallPass; ++t)
+        xv[t] = t0 + t < p.T ? __ldg(reinterpret_cast<const uint4*>(
+                                   p.x + static_cast<size_t>(t0 + t) * p.x_stride + k))
+                             : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int t = 0; t < kSmallPass; ++t) {
+        {
+          const uint32_t xw[4] = {xv[t].x, xv[t].y, xv[t].z, xv[t].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float lo = __uint_as_float(xw[q] << 16);
+            const float hi = __uint_as_float(xw[q] & 0xFFFF0000u);
+            acc[t] = fmaf(wv[2 * q], lo, acc[t]);
+            acc[t] = fmaf(wv[2 * q + 1], hi, acc[t]);
+            if (ss_warp) {
+              ss[t] = fmaf(lo, lo, ss[t]);
+              ss[t] = fmaf(hi, hi, ss[t]);
+            }
+          }
+        }
+      }
+    }
+    const float dot = reduce16(acc);
+    if ((lane & 1) == 0 && t0 + j < p.T && row_ok)
+      rb.logits_raw[(static_cast<size_t>(split) * p.T + t0 + j) * p.E + e] = dot;
+    if (ss_warp) {
+      const float sq = reduce16(ss);
+      if ((lane & 1) == 0 && t0 + j < p.T)
+        rb.sumsq[static_cast<size_t>(split) * p.T + t0 + j] = sq;
+    }
+  }
+}
+
 // Warp per token: combine the splits, apply the norm factor and bias, select.
 // With ss_from_x the row's sum of squares is taken from its bf16 input (the
 // tensor-core GEMM produces only the dots), else from the split partials.
@@ -461,7 +569,12 @@ __global__ void __launch_bounds__(256) router_topk_kernel(RouterParams p, RouteB
     }
     ssq = warp_sum(ssq);
   } else {
-    for (int s = 0; s < ksplit; ++s) ssq += rb.sumsq[static_cast<size_t>(s) * p.T + t];
+    float part[kMaxSplitParts];
+#pragma unroll
+    for (int s = 0; s < kMaxSplitParts; ++s)  // loads issued together
+      part[s] = s < ksplit ? __ldcg(rb.sumsq + static_cast<size_t>(s) * p.T + t) : 0.0f;
+#pragma unroll
+    for (int s = 0; s < kMaxSplitParts; ++s) ssq += part[s];
   }
   const float inv = p.norm ? rsqrtf(ssq / static_cast<float>(p.D) + p.eps) : 1.0f;
   if (lane == 0) rb.inv_rms[t] = inv;
@@ -542,6 +655,25 @@ cudaError_t launch_router_decode(const RouterParams& p, const RouteBuffers& rb, 
   return cudaGetLastError();
 }
 
+namespace {
+bool router_small_usable(const RouterParams& p) {
+  return p.T <= 64 && p.D % kSmallChunk == 0 && p.x_stride % 8 == 0 &&
+         (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(p.w) & 15u) == 0;
+}
+// Splits of whole 256-column chunks, at most kMaxSplitParts, enough for
+// about two CTAs per SM.
+int router_small_ksplit(int E, int D, int* chunks_per_split) {
+  const int nchunk = D / kSmallChunk;
+  const int row_ctas = (E + kSmallRows - 1) / kSmallRows;
+  int want = (296 + row_ctas - 1) / row_ctas;
+  want = want < 1 ? 1 : (want > kMaxSplitParts ? kMaxSplitParts : want);
+  if (want > nchunk) want = nchunk;
+  const int cps = (nchunk + want - 1) / want;
+  *chunks_per_split = cps;
+  return (nchunk + cps - 1) / cps;
+}
+}  // namespace
+
 cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s) {
   if (p.K > kMaxK || p.E > 512) return cudaErrorInvalidValue;
   const int mt = (p.T + kGBM - 1) / kGBM;
@@ -553,6 +685,12 @@ cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb,
     ksplit = router_tc_ksplit(p.T, p.E, p.D);
     from_x = 1;
     e = launch_router_tc(p, rb, ksplit, s);
+  } else if (router_small_usable(p)) {
+    int cps = 1;
+    ksplit = router_small_ksplit(p.E, p.D, &cps);
+    dim3 grid((p.E + kSmallRows - 1) / kSmallRows, ksplit);
+    router_small_kernel<<<grid, kSmallRows * 32, 0, s>>>(p, rb, cps);
+    e = cudaGetLastError();
   } else {
     while (mt * nt * ksplit < 148 && ksplit < 8 && p.D / (ksplit * 2) >= 256) ksplit *= 2;
     dim3 grid(mt, nt, ksplit);

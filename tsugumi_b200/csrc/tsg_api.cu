@@ -53,6 +53,7 @@ struct tsg_ctx_s {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   uint32_t decode_max_tokens = 4;
+  uint32_t gemv_max_tokens = 16;  // router-driven batches up to this size use the batched GEMVs
   std::string last_error;
   // workspace
   void* ws = nullptr;
@@ -409,9 +410,11 @@ bool fused_ok(tsg_ctx ctx, const tsg_moe_layer_s* L, uint32_t T) {
                            L->has_shared, ctx->num_sms);
 }
 
+// `routed`: the pairs come from this layer's router, so an expert holds at
+// most T rows (distinct experts per token) and every row tile has <= T rows.
 tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
                                uint32_t T, const float* residual, void* y, uint32_t y_stride,
-                               tsg_dtype y_dtype) {
+                               tsg_dtype y_dtype, bool routed = false) {
   // assumes rb.ids / rb.weights / rb.inv_rms are filled for T tokens
   const RouterParams rp = router_params(L, x, x_stride, T);
   const uint32_t K = L->desc.top_k;
@@ -419,13 +422,6 @@ tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, u
   TSG_CUDA_TRY(ctx, launch_permute(rp, ctx->rb, nullptr, ctx->stream), "permute");
   const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(L->desc.num_experts) * L->desc.d
                                     : nullptr;
-  TSG_CUDA_TRY(ctx,
-               launch_gather_rows_gate(static_cast<const uint16_t*>(x), x_stride, ctx->rb.inv_rms,
-                                       ctx->rb.sorted_pairs, static_cast<int>(P),
-                                       static_cast<int>(T), static_cast<int>(L->desc.d),
-                                       L->has_shared, ctx->xp, gate_w, ctx->rb.gate_raw,
-                                       ctx->stream),
-               "gather rows");
   const uint32_t rows = P + (L->has_shared ? T : 0u);
   QmmParams qp{};
   qp.D = static_cast<int>(L->desc.d);
@@ -441,10 +437,29 @@ tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, u
   qp.partials = ctx->partials;
   qp.err = ctx->rb.err;
   qp.num_sms = ctx->num_sms;
+  // few tokens per expert: batched GEMVs (the cost is the weight bytes);
+  // else the tcgen05 grouped contraction
+  const bool gemv = routed && T <= ctx->gemv_max_tokens &&
+                    T <= static_cast<uint32_t>(gemv_max_tile_rows()) && gemv_usable(qp);
+  TSG_CUDA_TRY(ctx,
+               launch_gather_rows_gate(static_cast<const uint16_t*>(x), x_stride, ctx->rb.inv_rms,
+                                       ctx->rb.sorted_pairs, static_cast<int>(P),
+                                       static_cast<int>(T), static_cast<int>(L->desc.d),
+                                       L->has_shared, ctx->xp, gate_w, ctx->rb.gate_raw,
+                                       ctx->stream, gemv ? 1 : 0),
+               "gather rows");
   prof_mark(ctx, 1);
-  TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, ctx->stream), "qmm gate/up");
+  if (gemv) {
+    TSG_CUDA_TRY(ctx, launch_gemv_gate_up(qp, static_cast<int>(T), ctx->stream), "gemv gate/up");
+  } else {
+    TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, ctx->stream), "qmm gate/up");
+  }
   prof_mark(ctx, 2);
-  TSG_CUDA_TRY(ctx, launch_qmm_down(qp, ctx->stream), "qmm down");
+  if (gemv) {
+    TSG_CUDA_TRY(ctx, launch_gemv_down(qp, static_cast<int>(T), ctx->stream), "gemv down");
+  } else {
+    TSG_CUDA_TRY(ctx, launch_qmm_down(qp, ctx->stream), "qmm down");
+  }
   prof_mark(ctx, 3);
   CombineParams cp{};
   cp.T = static_cast<int>(T);
@@ -697,6 +712,7 @@ tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char* name, int64_t value) {
   const std::string n(name);
   if (n == "fused_decode") ctx->use_fused = value != 0;
   else if (n == "programmatic_launch") ctx->allow_pdl = value != 0;
+  else if (n == "gemv_max_tokens") ctx->gemv_max_tokens = static_cast<uint32_t>(value < 0 ? 0 : value);
   else if (n == "debug_phase_stamps")
     ctx->stamps = reinterpret_cast<unsigned long long*>(static_cast<uintptr_t>(value));
   else return fail(ctx, TSG_ERR_INVALID_ARG, "unknown option " + n);
@@ -1093,7 +1109,8 @@ tsg_status tsg_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidde
     r = run_decode_experts(ctx, L, hidden, hidden_stride, T, residual, y, y_stride, y_dtype);
   } else {
     TSG_CUDA_TRY(ctx, launch_router_prefill(p, ctx->rb, ctx->stream), "router (prefill)");
-    r = run_prefill_experts(ctx, L, hidden, hidden_stride, T, residual, y, y_stride, y_dtype);
+    r = run_prefill_experts(ctx, L, hidden, hidden_stride, T, residual, y, y_stride, y_dtype,
+                            true);
   }
   if (ctx->profiling && ctx->prof_calls < ctx->prof_max) ++ctx->prof_calls;
   return r;

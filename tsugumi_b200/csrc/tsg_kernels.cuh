@@ -125,7 +125,7 @@ cudaError_t launch_make_pairs(const uint32_t* ids, const uint16_t* w_f16, int T,
 cudaError_t launch_gather_rows_gate(const uint16_t* x, uint32_t x_stride, const float* inv_rms,
                                     const Pair* sorted_pairs, int n_rows, int T, int D,
                                     int append_tokens, __half* xp, const float* gate_w,
-                                    float* gate_raw, cudaStream_t s);
+                                    float* gate_raw, cudaStream_t s, int frag_order = 0);
 
 // decode.cu
 struct DecodeParams {
@@ -200,6 +200,13 @@ struct QmmParams {
 cudaError_t launch_qmm_gate_up(const QmmParams& p, cudaStream_t s);
 cudaError_t launch_qmm_down(const QmmParams& p, cudaStream_t s);
 int qmm_tile_rows();
+
+// gemv.cu: the same products as batched GEMVs for row tiles of at most
+// max_rows <= 64 rows
+cudaError_t launch_gemv_gate_up(const QmmParams& p, int max_rows, cudaStream_t s);
+cudaError_t launch_gemv_down(const QmmParams& p, int max_rows, cudaStream_t s);
+int gemv_max_tile_rows();
+bool gemv_usable(const QmmParams& p);  // D % 128 == 0, F % 64 == 0, aligned scales
 
 // combine.cu
 struct CombineParams {
