@@ -55,19 +55,6 @@ __global__ void place_pairs_kernel(const Pair* pairs, int n, int T, int K, int E
 }
 
 // ---- 2. counts + last-CTA scan ---------------------------------------------
-__device__ uint32_t block_sum_u32(uint32_t v, uint32_t* s_tmp) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-  if (lane == 0) s_tmp[warp] = v;
-  __syncthreads();
-  uint32_t r = 0;
-  if (threadIdx.x == 0)
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) r += s_tmp[w];
-  __syncthreads();
-  return r;  // valid in thread 0
-}
-
 // Exclusive scan of v over the block (thread order); returns the prefix and
 // writes the block total to *total.
 __device__ uint32_t block_excl_scan(uint32_t v, uint32_t* s_tmp, uint32_t* total) {
@@ -124,24 +111,11 @@ __global__ void __launch_bounds__(kThreads) permute_hist_kernel(PermuteArgs a, R
 }
 
 // ---- 2. prefixes, counts, expert order, groups and schedules ----------------
-__global__ void __launch_bounds__(kScanThreads) permute_scan_kernel(PermuteArgs a, RouteBuffers rb,
-                                                                    int n_chunks) {
-  __shared__ uint32_t s_tmp[33];
-  extern __shared__ uint32_t s_dyn[];  // [3 * E]
-  uint32_t* s_cnt = s_dyn;  // [E]
-  // each thread turns one expert's column of chunk counts into prefixes
-  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
-    uint32_t run = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      uint32_t* h = rb.hist + static_cast<size_t>(c) * a.E + e;
-      const uint32_t v = *h;
-      *h = run;
-      run += v;
-    }
-    s_cnt[e] = run;
-    rb.counts[e] = run;
-  }
-  __syncthreads();
+// From the per-expert counts in s_dyn[0, E): the expert order, offsets,
+// groups, tiles and row tiles.  s_dyn holds 3 E words.
+TSG_DEV void order_and_schedule(const PermuteArgs& a, const RouteBuffers& rb, uint32_t* s_dyn,
+                                   uint32_t* s_tmp) {
+  uint32_t* s_cnt = s_dyn;
   const int E = a.E;
   uint32_t* s_order = s_dyn + E;    // [E] order position -> expert
   uint32_t* s_rank = s_dyn + 2 * E; // [E] expert -> order position
@@ -228,21 +202,43 @@ __global__ void __launch_bounds__(kScanThreads) permute_scan_kernel(PermuteArgs 
   }
 }
 
+__global__ void __launch_bounds__(kScanThreads) permute_scan_kernel(PermuteArgs a, RouteBuffers rb,
+                                                                    int n_chunks) {
+  __shared__ uint32_t s_tmp[33];
+  extern __shared__ uint32_t s_dyn[];  // [3 * E]
+  // each thread turns one expert's column of chunk counts into prefixes
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+    uint32_t run = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+      uint32_t* h = rb.hist + static_cast<size_t>(c) * a.E + e;
+      const uint32_t v = *h;
+      *h = run;
+      run += v;
+    }
+    s_dyn[e] = run;
+    rb.counts[e] = run;
+  }
+  __syncthreads();
+  order_and_schedule(a, rb, s_dyn, s_tmp);
+}
+
 // ---- 3. stable scatter -----------------------------------------------------
-__global__ void __launch_bounds__(kThreads) permute_scatter_kernel(PermuteArgs a, RouteBuffers rb,
-                                                                  const uint16_t* tm_w16,
-                                                                  const float* w_f32) {
-  extern __shared__ uint32_t s_dyn[];
+// Chunk c of NTHREADS-thread rounds; s_dyn holds (2 + NTHREADS / 32) E words.
+// `chunk_prefix`: the chunk's per-expert prefixes in rb.hist (else zero).
+template <int NTHREADS>
+TSG_DEV void scatter_chunk(const PermuteArgs& a, const RouteBuffers& rb, const uint16_t* tm_w16,
+                              const float* w_f32, int c, bool chunk_prefix, uint32_t* s_dyn) {
   const int E = a.E;
   uint32_t* s_base = s_dyn;          // [E] sorted position of this chunk's first pair of e
   uint32_t* s_run = s_dyn + E;       // [E] pairs of e already placed by this chunk
-  uint32_t* s_wc = s_dyn + 2 * E;    // [kThreads / 32][E] per-warp counts of the sub-block
-  const int c = blockIdx.x;
+  uint32_t* s_wc = s_dyn + 2 * E;    // [NTHREADS / 32][E] per-warp counts of the sub-block
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kWarps = kThreads / 32;
+  constexpr int kWarps = NTHREADS / 32;
+  constexpr int kThreads = NTHREADS;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const uint32_t off = __ldcg(rb.offsets + e);
-    s_base[e] = off + rb.hist[static_cast<size_t>(c) * E + e];  // unused when e is empty
+    // unused when e is empty
+    s_base[e] = off + (chunk_prefix ? rb.hist[static_cast<size_t>(c) * E + e] : 0u);
     s_run[e] = 0u;
   }
   for (int x = threadIdx.x; x < kWarps * E; x += blockDim.x) s_wc[x] = 0u;
@@ -284,6 +280,34 @@ __global__ void __launch_bounds__(kThreads) permute_scatter_kernel(PermuteArgs a
     if (valid && lt == 0u) s_wc[warp * E + id] = 0u;
     __syncthreads();
   }
+}
+
+__global__ void __launch_bounds__(kThreads) permute_scatter_kernel(PermuteArgs a, RouteBuffers rb,
+                                                                  const uint16_t* tm_w16,
+                                                                  const float* w_f32) {
+  extern __shared__ uint32_t s_dyn[];
+  scatter_chunk<kThreads>(a, rb, tm_w16, w_f32, static_cast<int>(blockIdx.x), true, s_dyn);
+}
+
+// All three steps in one CTA when the pairs fit one chunk (small batches):
+// counts in shared memory, then the same ordering, schedules and scatter.
+__global__ void __launch_bounds__(kScanThreads) permute_small_kernel(PermuteArgs a, RouteBuffers rb,
+                                                                     const uint16_t* tm_w16,
+                                                                     const float* w_f32) {
+  __shared__ uint32_t s_tmp[33];
+  extern __shared__ uint32_t s_dyn[];
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) s_dyn[e] = 0u;
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.P; i += blockDim.x) {
+    const uint32_t id = a.tm_ids[i];
+    if (id < static_cast<uint32_t>(a.E)) atomicAdd(&s_dyn[id], 1u);
+    else record_error(rb.err, 8u, id);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) rb.counts[e] = s_dyn[e];
+  order_and_schedule(a, rb, s_dyn, s_tmp);
+  __syncthreads();  // offsets (global, this CTA's writes) are read below
+  scatter_chunk<kScanThreads>(a, rb, tm_w16, w_f32, 0, false, s_dyn);
 }
 
 __global__ void make_pairs_kernel(const uint32_t* ids, const uint16_t* w16, int T, int K,
@@ -381,6 +405,15 @@ cudaError_t launch_permute(const RouterParams& p, const RouteBuffers& rb, const 
   a.has_shared = p.has_shared;
   a.sort_keys = p.sort_keys;
   const int n_chunks = permute_chunks(P);
+  if (n_chunks == 1) {
+    const size_t smem = (2u + kScanThreads / 32) * p.E * sizeof(uint32_t);
+    if (smem > 48u * 1024u) {
+      const cudaError_t e = allow_max_smem(permute_small_kernel);
+      if (e != cudaSuccess) return e;
+    }
+    permute_small_kernel<<<1, kScanThreads, smem, s>>>(a, rb, w16, rb.weights);
+    return cudaGetLastError();
+  }
   permute_hist_kernel<<<n_chunks, kThreads, p.E * sizeof(uint32_t), s>>>(a, rb);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
