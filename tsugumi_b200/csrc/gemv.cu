@@ -68,15 +68,45 @@ struct GemvArgs {
   uint32_t* err;
 };
 
-TSG_DEV void cp_async16(uint32_t dst, const void* src, bool ok) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(ok ? 16 : 0)
+// cp.async of 16 / 4 bytes to shared address dst + OFF; the "z" forms copy
+// `n` source bytes (0 or the full size) and zero-fill the rest.
+template <int OFF>
+TSG_DEV void cp16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0+%2], [%1], 16;" ::"r"(dst), "l"(src), "n"(OFF)
                : "memory");
 }
-TSG_DEV void cp_async4(uint32_t dst, const void* src, bool ok) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
-               "r"(ok ? 4 : 0)
+template <int OFF>
+TSG_DEV void cp16z(uint32_t dst, const void* src, uint32_t n) {
+  asm volatile("cp.async.cg.shared.global [%0+%3], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n),
+               "n"(OFF)
                : "memory");
+}
+TSG_DEV void cp4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+TSG_DEV void cp4z(uint32_t dst, const void* src, uint32_t n) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(n)
+               : "memory");
+}
+TSG_DEV uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+TSG_DEV uint4 lds128_512(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+512];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+TSG_DEV void lds_scale_pair(uint32_t addr, __half* a, __half* b) {
+  unsigned short x, y;
+  asm volatile("ld.shared.u16 %0, [%2];\n\tld.shared.u16 %1, [%2+8];" : "=h"(x), "=h"(y) : "r"(addr));
+  *a = __ushort_as_half(x);
+  *b = __ushort_as_half(y);
 }
 TSG_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -129,22 +159,21 @@ TSG_DEV Cursor item_cursor(const GemvArgs& a, uint32_t item, int per_tile, int g
 
 // Copies the cursor's super-group into a ring slot (codes of rows a and b at
 // lane * 16 and 512 + lane * 16; scales at 1024 + g * 16: a's four groups,
-// then b's) and advances it.  Groups past the row end (an even count) are
+// then b's) and advances it.  `dst` is the slot + lane * 16, `sdst` the
+// lane's scale destination.  Groups past the row end (an even count) are
 // zero-filled from a valid address in the row: a zero scale and zero tokens
 // make them contribute nothing.
-TSG_DEV void issue_step(uint32_t slot, Cursor& r, int lane) {
-  const int g = lane >> 2, c = lane & 3;
-  const uint32_t sdst = slot + 1024 + g * 16 + (c & 1) * 8 + (c & 2) * 2;
+TSG_DEV void issue_step(uint32_t dst, uint32_t sdst, Cursor& r, int c) {
   if (r.left >= 4) {  // warp-uniform: a whole super-group
-    cp_async16(slot + lane * 16, r.ca, true);
-    cp_async16(slot + 512 + lane * 16, r.cb, true);
-    cp_async4(sdst, r.sc, true);
+    cp16<0>(dst, r.ca);
+    cp16<512>(dst, r.cb);
+    cp4(sdst, r.sc);
   } else {
     const bool okc = c < r.left;
     const bool oks = (c & 2) < r.left;
-    cp_async16(slot + lane * 16, okc ? r.ca : r.ca - 16 * c, okc);
-    cp_async16(slot + 512 + lane * 16, okc ? r.cb : r.cb - 16 * c, okc);
-    cp_async4(sdst, oks ? r.sc : r.sc - (c & 2), oks);
+    cp16z<0>(dst, okc ? r.ca : r.ca - 16 * c, okc ? 16u : 0u);
+    cp16z<512>(dst, okc ? r.cb : r.cb - 16 * c, okc ? 16u : 0u);
+    cp4z(sdst, oks ? r.sc : r.sc - (c & 2), oks ? 4u : 0u);
   }
   r.ca += 64;
   r.cb += 64;
@@ -193,8 +222,7 @@ TSG_DEV void super_group(float (&acc)[MAXB][CH][4], const uint4& ra, const uint4
 
 TSG_DEV void split_scale(__half s, __half2* s2, __half2* s16) {
   *s2 = __halves2half2(s, s);
-  const __half q = __hmul(s, __float2half_rn(0.0625f));
-  *s16 = __halves2half2(q, q);
+  *s16 = __hmul2(*s2, bits_h2(0x2C002C00u));  // (s / 16, s / 16), exact
 }
 
 template <int MODE, int ACT, int MAXB>
@@ -218,30 +246,35 @@ __global__ void __launch_bounds__(GemvShape<MAXB>::kThreads, 1) gemv_kernel(cons
   const uint32_t hi = static_cast<uint32_t>(
       static_cast<uint64_t>(n_items) * (blockIdx.x + 1) / gridDim.x);
   const __half* bsrc = MODE == 0 ? a.xp : a.act_buf;
-  uint8_t* ring = gemv_smem + warp * S::kWarpRing;
-  const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
+  // the lane's addresses in the warp's ring: slot + lane * 16, advancing by
+  // one slot per step and wrapping; scale destination and source offsets
+  const uint32_t ring_lane =
+      static_cast<uint32_t>(__cvta_generic_to_shared(gemv_smem + warp * S::kWarpRing)) + lane * 16;
+  const uint32_t ring_end = ring_lane + kStages * kSlotBytes;
+  const uint32_t s_put = 1024 + g * 16 + (c & 1) * 8 + (c & 2) * 2 - lane * 16;
+  const uint32_t s_get = 1024 + g * 16 + c * 2 - lane * 16;
 
   // producer cursor: runs kStages - 1 steps ahead of the consumer
   uint32_t p_item = lo + warp;
-  int p_s = 0, p_slot = 0;
+  uint32_t p_slot = ring_lane;
   Cursor pr{};
   if (p_item < hi) pr = item_cursor<MODE>(a, p_item, per_tile, g, c, ngroups);
   auto produce = [&]() {
     if (p_item < hi) {
-      issue_step(ring_s + p_slot * kSlotBytes, pr, lane);
-      if (++p_s == nsg) {
-        p_s = 0;
+      issue_step(p_slot, p_slot + s_put, pr, c);
+      if (pr.left <= 0) {
         p_item += kWarps;
         if (p_item < hi) pr = item_cursor<MODE>(a, p_item, per_tile, g, c, ngroups);
       }
     }
     cp_async_commit();  // an empty group keeps the count uniform
-    p_slot = p_slot + 1 == kStages ? 0 : p_slot + 1;
+    p_slot += kSlotBytes;
+    if (p_slot == ring_end) p_slot = ring_lane;
   };
 #pragma unroll 1
   for (int i = 0; i < kStages - 1; ++i) produce();
 
-  int c_slot = 0;
+  uint32_t c_slot = ring_lane;
   for (uint32_t item = lo + warp; item < hi; item += kWarps) {
     const uint32_t t = item / static_cast<uint32_t>(per_tile);
     const int sub = static_cast<int>(item - t * static_cast<uint32_t>(per_tile));
@@ -266,12 +299,12 @@ __global__ void __launch_bounds__(GemvShape<MAXB>::kThreads, 1) gemv_kernel(cons
     for (int s = 0; s < nsg; ++s) {
       produce();
       cp_async_wait<kStages - 1>();  // this step's slot has landed
-      const uint8_t* slot = ring + c_slot * kSlotBytes;
-      c_slot = c_slot + 1 == kStages ? 0 : c_slot + 1;
-      const uint4 ra = *reinterpret_cast<const uint4*>(slot + lane * 16);
-      const uint4 rb = *reinterpret_cast<const uint4*>(slot + 512 + lane * 16);
-      const __half sa = *reinterpret_cast<const __half*>(slot + 1024 + g * 16 + c * 2);
-      const __half sb = *reinterpret_cast<const __half*>(slot + 1024 + g * 16 + 8 + c * 2);
+      const uint4 ra = lds128(c_slot);
+      const uint4 rb = lds128_512(c_slot);
+      __half sa, sb;
+      lds_scale_pair(c_slot + s_get, &sa, &sb);
+      c_slot += kSlotBytes;
+      if (c_slot == ring_end) c_slot = ring_lane;
       __half2 sa2, sa16, sb2, sb16;
       split_scale(sa, &sa2, &sa16);
       split_scale(sb, &sb2, &sb16);

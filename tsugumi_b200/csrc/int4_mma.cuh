@@ -44,8 +44,8 @@ TSG_DEV __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 // s2 = (s, s), s16 = (s / 16, s / 16).
 TSG_DEV void dequant_word(uint32_t w, __half2 s2, __half2 s16, uint32_t (&p)[4]) {
   const uint32_t w8 = w >> 8;
-  const __half2 lo_off = __floats2half2_rn(1032.0f, 1032.0f);
-  const __half2 hi_off = __floats2half2_rn(1152.0f, 1152.0f);
+  const __half2 lo_off = bits_h2(0x64086408u);  // (1032, 1032)
+  const __half2 hi_off = bits_h2(0x64806480u);  // (1152, 1152)
   p[0] = h2_bits(__hmul2(__hsub2(bits_h2(and_or(w, 0x000F000Fu, 0x64006400u)), lo_off), s2));
   p[1] = h2_bits(__hmul2(__hsub2(bits_h2(and_or(w8, 0x000F000Fu, 0x64006400u)), lo_off), s2));
   p[2] = h2_bits(__hmul2(__hsub2(bits_h2(and_or(w, 0x00F000F0u, 0x64006400u)), hi_off), s16));
@@ -55,8 +55,7 @@ TSG_DEV void dequant_word(uint32_t w, __half2 s2, __half2 s16, uint32_t (&p)[4])
 TSG_DEV void scale_pair(const __half* s, __half2* s2, __half2* s16) {
   const __half h = *s;
   *s2 = __halves2half2(h, h);
-  const __half q = __hmul(h, __float2half_rn(0.0625f));
-  *s16 = __halves2half2(q, q);
+  *s16 = __hmul2(*s2, bits_h2(0x2C002C00u));  // (s / 16, s / 16), exact
 }
 
 // Eight consecutive fp16 values (one 16-byte load, natural order) as the B
