@@ -667,6 +667,8 @@ def run_ncu_case(args):
     """A short fixed workload for profiling under ncu (prints nothing timed):
     decode-t1  the 30-layer Gemma-like stack at T=1, 8 passes, on 4 layers
                (the first 2 passes warm up; capture with -s 8 -c 1..3);
+    small-t16  4 Gemma-like layers at T=16 (batched-GEMV regime), 4 passes,
+               the same random input into every layer;
     prefill    one Gemma-like layer at T=4096 with Zipf(1.1) skew, 3 passes."""
     import torch
     import tsugumi_b200 as tb
@@ -683,6 +685,14 @@ def run_ncu_case(args):
         for _ in range(8):
             for lay in layers:
                 x = lay.forward(x)
+    elif args.ncu_case == "small-t16":
+        layers = [tb.MoELayer(ctx, device_layer_tensors(CFG, 1 + 7919 * l, None, device))
+                  for l in range(4)]
+        x = torch.randn((16, D), device=device).to(torch.bfloat16)
+        ctx.reserve(layers[0], 64)
+        for _ in range(4):
+            for lay in layers:
+                lay.forward(x)
     else:
         layer = tb.MoELayer(ctx, device_layer_tensors(CFG, 91, 1.1, device))
         x = torch.randn((4096, D), device=device).to(torch.bfloat16)
@@ -703,7 +713,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--pdl", action="store_true", help="allow programmatic dependent launch")
-    ap.add_argument("--ncu-case", choices=["decode-t1", "prefill"], default=None,
+    ap.add_argument("--ncu-case", choices=["decode-t1", "small-t16", "prefill"], default=None,
                     help="run a short fixed workload for ncu instead of the benchmark")
     args = ap.parse_args()
     if args.warmup < 3:

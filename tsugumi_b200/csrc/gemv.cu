@@ -114,6 +114,18 @@ TSG_DEV void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// The row tiles of a CTA's item range, staged in shared memory at the start
+// (an item switch then costs no global-memory round trip); ranges over more
+// tiles than the cache holds read the rest from global memory.
+constexpr int kTileCache = 32;
+struct TileCache {
+  const RowTile* s;  // shared memory
+  uint32_t t0, n;
+  TSG_DEV RowTile get(const GemvArgs& a, uint32_t t) const {
+    return t - t0 < n ? s[t - t0] : a.tiles[t];
+  }
+};
+
 // The producer's copy cursor for one item: the lane's code group 4 s + c of
 // weight rows a = g and b = g + 8 of the item's 16-row MMA block, its scale
 // pair (groups 4 s + (c & 2), + 1; of row a for even c, of row b for odd c)
@@ -126,11 +138,11 @@ struct Cursor {
 };
 
 template <int MODE>
-TSG_DEV Cursor item_cursor(const GemvArgs& a, uint32_t item, int per_tile, int g, int c,
-                           int ngroups) {
+TSG_DEV Cursor item_cursor(const GemvArgs& a, const TileCache& tc, uint32_t item, int per_tile,
+                           int g, int c, int ngroups) {
   const uint32_t t = item / static_cast<uint32_t>(per_tile);
   const int sub = static_cast<int>(item - t * static_cast<uint32_t>(per_tile));
-  const uint32_t expert = __ldg(&a.tiles[t].expert);
+  const uint32_t expert = tc.get(a, t).expert;
   const bool sh = expert >= static_cast<uint32_t>(a.E);
   const ExpertOffsets& o = sh ? a.soff : a.off;
   const uint8_t* blob = sh ? a.shared : a.ebase + static_cast<uint64_t>(expert) * a.estride;
@@ -246,6 +258,14 @@ __global__ void __launch_bounds__(GemvShape<MAXB>::kThreads, 1) gemv_kernel(cons
   const uint32_t hi = static_cast<uint32_t>(
       static_cast<uint64_t>(n_items) * (blockIdx.x + 1) / gridDim.x);
   const __half* bsrc = MODE == 0 ? a.xp : a.act_buf;
+  __shared__ RowTile s_tiles[kTileCache];
+  TileCache tc;
+  tc.s = s_tiles;
+  tc.t0 = lo / static_cast<uint32_t>(per_tile);
+  tc.n = hi > lo ? (hi - 1) / static_cast<uint32_t>(per_tile) - tc.t0 + 1 : 0u;
+  if (tc.n > static_cast<uint32_t>(kTileCache)) tc.n = kTileCache;
+  if (threadIdx.x < tc.n) s_tiles[threadIdx.x] = a.tiles[tc.t0 + threadIdx.x];
+  __syncthreads();
   // the lane's addresses in the warp's ring: slot + lane * 16, advancing by
   // one slot per step and wrapping; scale destination and source offsets
   const uint32_t ring_lane =
@@ -258,13 +278,13 @@ __global__ void __launch_bounds__(GemvShape<MAXB>::kThreads, 1) gemv_kernel(cons
   uint32_t p_item = lo + warp;
   uint32_t p_slot = ring_lane;
   Cursor pr{};
-  if (p_item < hi) pr = item_cursor<MODE>(a, p_item, per_tile, g, c, ngroups);
+  if (p_item < hi) pr = item_cursor<MODE>(a, tc, p_item, per_tile, g, c, ngroups);
   auto produce = [&]() {
     if (p_item < hi) {
       issue_step(p_slot, p_slot + s_put, pr, c);
       if (pr.left <= 0) {
         p_item += kWarps;
-        if (p_item < hi) pr = item_cursor<MODE>(a, p_item, per_tile, g, c, ngroups);
+        if (p_item < hi) pr = item_cursor<MODE>(a, tc, p_item, per_tile, g, c, ngroups);
       }
     }
     cp_async_commit();  // an empty group keeps the count uniform
@@ -278,7 +298,7 @@ __global__ void __launch_bounds__(GemvShape<MAXB>::kThreads, 1) gemv_kernel(cons
   for (uint32_t item = lo + warp; item < hi; item += kWarps) {
     const uint32_t t = item / static_cast<uint32_t>(per_tile);
     const int sub = static_cast<int>(item - t * static_cast<uint32_t>(per_tile));
-    const RowTile tile = a.tiles[t];
+    const RowTile tile = tc.get(a, t);
     const bool bad = static_cast<int>(tile.rows) > 8 * MAXB;
     if (bad && lane == 0) flag_error(a.err, TSG_DEVERR_BOUNDS);  // the host keeps tiles <= 64 rows
     const int cnt = bad ? 0 : static_cast<int>(tile.rows);
