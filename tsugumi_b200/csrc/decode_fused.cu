@@ -16,8 +16,8 @@
 //             and keeps them as fp16 MMA fragments; it then publishes the raw
 //             dots of its router rows as (launch tag, value) words;
 //   select    every CTA reads all logits of the launch (polling their tags)
-//             and selects the top K of each token itself: one thread per
-//             logit counts the logits ordered before it (larger value, or
+//             and selects the top K of each token itself: four lanes per
+//             logit count the logits ordered before it (larger value, or
 //             equal value and smaller index: the reference's order and tie
 //             rule), and ranks below K are the selection in slot order; the
 //             pairs are grouped by expert with a 32-lane bitonic sort;
@@ -582,20 +582,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the rank of a logit is the number of logits ordered before it (larger
     // key, or equal key and smaller index: the reference's order and tie
     // rule); ranks below K are the selection, in slot order
+    // four lanes per logit, each counting every fourth run of 4 keys; the
+    // quad's counts are summed with two shuffles
     const float inv_e = 1.0f / static_cast<float>(E);
-    for (int q = tid; q < T * E; q += kThreads) {
-      const int t = qdiv(q, inv_e), e = q - t * E;
+    for (int base = warp * 8; base < T * E; base += kWarps * 8) {
+      const int q = base + (lane >> 2), part = lane & 3;
+      const bool valid = q < T * E;
+      const int qq = valid ? q : 0;
+      const int t = qdiv(qq, inv_e), e = qq - t * E;
       const uint32_t* row = s_key + t * E;
       const uint32_t ke = row[e];
       int rank = 0;
-      for (int e2 = 0; e2 < E; e2 += 4) {
+      for (int e2 = part * 4; e2 < E; e2 += 16) {
         const uint4 k4 = *reinterpret_cast<const uint4*>(row + e2);
         rank += (k4.x > ke || (k4.x == ke && e2 < e)) ? 1 : 0;
         rank += (k4.y > ke || (k4.y == ke && e2 + 1 < e)) ? 1 : 0;
         rank += (k4.z > ke || (k4.z == ke && e2 + 2 < e)) ? 1 : 0;
         rank += (k4.w > ke || (k4.w == ke && e2 + 3 < e)) ? 1 : 0;
       }
-      if (rank < K) {
+      __syncwarp();
+      rank += __shfl_xor_sync(0xFFFFFFFFu, rank, 1);
+      rank += __shfl_xor_sync(0xFFFFFFFFu, rank, 2);
+      if (valid && part == 0 && rank < K) {
         s_ids[t][rank] = e;
         s_sc[t][rank] = key_value(ke);
       }
