@@ -22,12 +22,14 @@
 //            (f, token) pair and writes act = act_fn(g) * u as fp16;
 //   down     item = (row tile, 16 output rows d): partials[row][d] in fp16,
 //            which the combine kernel reads as for the tensor-core path.
-// The weight stream is what bounds the kernel, so each warp keeps kStages
-// super-groups of codes and scales in flight: cp.async copies (16 bytes of
-// codes per lane and row, 4 bytes of scales) into a ring in shared memory
-// that only the copying lane reads back, issued kStages - 1 steps ahead
-// across item boundaries.  A CTA takes a contiguous range of items, so its
-// warps mostly share a row tile and read its token rows from L1.
+// To cover DRAM latency each warp keeps kStages super-groups of codes and
+// scales in flight: cp.async copies (16 bytes of codes per lane and row, 4
+// bytes of scales) into a ring in shared memory that only the copying lane
+// reads back, issued kStages - 1 steps ahead across item boundaries.  With
+// that, instruction issue bounds the kernel (~200 instructions per warp and
+// KB of codes, 96 of them the exact dequantisation), not the weight stream.
+// A CTA takes a contiguous range of items, so its warps mostly share a row
+// tile and read its token rows from L1.
 #include "int4_mma.cuh"
 #include "tsg_common.cuh"
 #include "tsg_kernels.cuh"
