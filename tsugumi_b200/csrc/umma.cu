@@ -61,12 +61,11 @@ constexpr int kBStageBytes = kStageK * kBBytes;
 constexpr int kAStages = 2;            // A ring in TMEM (2 x 64 columns after the accumulators)
 constexpr int kMaxBStages = 3;         // B ring in shared memory
 constexpr int kMaxCodeStages = 8;
-constexpr int kThreadsQ = 28 * 32;
+constexpr int kThreadsQ = 27 * 32;
 constexpr int kEpiWarp1 = 23;          // warps 0-3 and 23-26 drain the accumulators
 constexpr int kEpiWarps = 8;
 constexpr int kCodeWarp = 5;
 constexpr int kMmaWarp = 6;   // shares its SMSP with epilogue warp 2, which only hands values over
-constexpr int kMmaWarp2 = 27; // issues the odd k-step of every stage (SMSP 3)
 constexpr int kDqWarp0 = 7;
 constexpr int kNumDqWarps = 16;
 constexpr uint32_t kTmemCols = 512;
@@ -180,11 +179,11 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
   if (tid == 0) {
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(&sm.full_a[s], kNumDqWarps);
-      mbar_init(&sm.empty_a[s], 2);  // one commit per MMA issuer
+      mbar_init(&sm.empty_a[s], 1);
     }
     for (int s = 0; s < SB; ++s) {
       mbar_init(&sm.full_b[s], 1);
-      mbar_init(&sm.empty_b[s], 2);
+      mbar_init(&sm.empty_b[s], 1);
     }
     for (int c = 0; c < C; ++c) {
       mbar_init(&sm.full_c[c], 1);
@@ -193,7 +192,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.full_s[i], 1);
       mbar_init(&sm.empty_s[i], kNumDqWarps);
-      mbar_init(&sm.tmem_full[i], 2);
+      mbar_init(&sm.tmem_full[i], 1);
       mbar_init(&sm.tmem_empty[i], kEpiWarps);
     }
     fence_mbar_init();
@@ -206,18 +205,6 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
-  // Both MMA issuers accumulate into a zeroed accumulator (neither knows
-  // whether the other's MMAs came first), so the epilogue warps zero both
-  // accumulators here and every drained column afterwards.
-  if (warp < 4 || (warp >= kEpiWarp1 && warp < kEpiWarp1 + 4)) {
-    const uint32_t zq = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
-    const uint32_t zero[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-    for (uint32_t c0 = warp < 4 ? 0u : 16u; c0 < kAccCols; c0 += 32) tmem_st16(zq + c0, zero);
-    tmem_st_wait();
-  }
-  tc_fence_before_sync();
-  __syncthreads();
-  tc_fence_after_sync();
 
   // number of items this CTA owns
   uint32_t my_items = 0;
@@ -321,14 +308,9 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       for (uint32_t q = (scales_issued > 2 ? scales_issued - 2 : 0); q < scales_issued; ++q)
         mbar_sleep(&sm.full_s[q & 1u], (q >> 1) & 1u, err);
     }
-  } else if (warp == kMmaWarp || warp == kMmaWarp2) {
-    // ---------------- MMA issuers ----------------
-    // One thread issues a tcgen05.mma only every ~100-150 cycles whatever
-    // its N, so two threads on different SMSPs share each stage: warp 6 the
-    // even k-step, warp 27 the odd one, into the same (zeroed) accumulator.
-    // Both commit to every barrier they release (each counts two arrivals).
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const bool odd = warp == kMmaWarp2;
       Ring ra, rb;  // A ring (TMEM), B ring (shared memory)
       bool ok = true;
       for (uint32_t i = 0; i < my_items && ok; ++i) {
@@ -349,9 +331,8 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
           tc_fence_after_sync();
           const uint32_t a_tmem = tmem + kAccCols + static_cast<uint32_t>(ra.s) * kAStageCols;
           const uint32_t b0 = smem_u32(stage_b(rb.s));
-          if (!odd)
-            umma_f16_ts_k64(d_tmem, a_tmem, umma_desc_sw128(b0), idesc, 1u);
-          else if (kStageK * j + 1 < ksteps)
+          umma_f16_ts_k64(d_tmem, a_tmem, umma_desc_sw128(b0), idesc, j > 0 ? 1u : 0u);
+          if (kStageK * j + 1 < ksteps)
             umma_f16_ts_k64(d_tmem, a_tmem + kAKStepCols, umma_desc_sw128(b0 + kBBytes), idesc, 1u);
           // look at the next stage's barriers before the commits, so that
           // the answer is back by the time the loop needs it
@@ -463,7 +444,7 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.full_a[pend]);
     }
-  } else if (warp < 4 || (warp >= kEpiWarp1 && warp < kEpiWarp1 + 4)) {
+  } else if (warp < 4 || warp >= kEpiWarp1) {
     // ---------------- epilogue: warps 0-3 and 23-26 ----------------
     // Two warps per TMEM lane quarter (q = warp % 4), taking alternate
     // 16-column chunks.  A failed wait does not leave the loop: the warp
@@ -478,12 +459,10 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       tc_fence_after_sync();
       const uint32_t n = (w.rows + 15u) & ~15u;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(32 * q) << 16) + acc * kTileN;
-      const uint32_t zero[16] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
       for (uint32_t c0 = c_first; ok && c0 < n; c0 += 32) {
         uint32_t r[16];
         tmem_ld16(tbase + c0, r);
         tmem_ld_wait();
-        tmem_st16(tbase + c0, zero);  // ready for the next item's accumulation
         if (MODE == 0) {
           // lane l < 16 holds gate(f, c0 + j), lane l + 16 up(f, c0 + j).  The
           // low half-warp finishes columns c0..c0+7, the high half c0+8..c0+15:
@@ -513,7 +492,6 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
           }
         }
       }
-      tmem_st_wait();
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.tmem_empty[acc]);
