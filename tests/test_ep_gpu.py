@@ -46,6 +46,9 @@ def _rank_main(rank: int, port: int, q):
         dev = torch.device("cuda", rank)
         ctx = tb.Context(rank)
         ctx.set_stream(torch.cuda.current_stream())
+        # the expert-parallel path runs the tensor-core contraction for every
+        # batch; the single-GPU reference must too (not the batched GEMVs)
+        ctx.set_option("gemv_max_tokens", 0)
         group = ep.ExpertParallelGroup.from_torch_distributed(ctx)
         msgs = []
         for name, T, skew in CASES:
