@@ -42,12 +42,13 @@ constexpr int kMaxBlk = 8;  // token column blocks of 8: up to 64 rows per tile
 // the scales, 16 bytes per row pair g: a's four groups, b's four groups
 constexpr int kSlotBytes = 1024 + 128;
 
-// Launch shape by the largest tile (MAXB token blocks): few blocks leave
-// registers for more warps and two accumulator chains per block (the MMAs
-// of a super-group alternate between them), many blocks need the registers.
+// Launch shape by the largest tile (MAXB token blocks): 16 warps per CTA
+// (measured: 576 or 640 threads were slower, and 576 spilled at B = 2); one
+// token block leaves registers for two accumulator chains (the MMAs of a
+// super-group alternate between them).
 template <int MAXB>
 struct GemvShape {
-  static constexpr int kThreads = MAXB == 1 ? 640 : (MAXB == 2 ? 576 : 512);
+  static constexpr int kThreads = 512;
   static constexpr int kWarps = kThreads / 32;
   static constexpr int kStages = MAXB <= 2 ? 6 : 8;  // super-groups in flight per warp
   static constexpr int kChains = MAXB == 1 ? 2 : 1;
