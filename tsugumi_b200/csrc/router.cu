@@ -704,13 +704,6 @@ cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb,
   return cudaGetLastError();
 }
 
-int router_prefill_ksplit(int T, int E, int D) {
-  const int mt = (T + kGBM - 1) / kGBM;
-  const int nt = (E + kGBN - 1) / kGBN;
-  int ksplit = 1;
-  while (mt * nt * ksplit < 148 && ksplit < 8 && D / (ksplit * 2) >= 256) ksplit *= 2;
-  return ksplit;
-}
 
 }  // namespace tsg
 

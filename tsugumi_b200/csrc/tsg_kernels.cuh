@@ -105,7 +105,6 @@ cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb,
 cudaError_t launch_rowprep(const RouterParams& p, const RouteBuffers& rb, int write_rows,
                            cudaStream_t s);
 cudaError_t launch_group_small(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s);
-int router_prefill_ksplit(int T, int E, int D);
 
 // router_tc.cu: the prefill router GEMM on tcgen05 (exact fp32 through three
 // bf16 planes of the router rows, made once per layer)
