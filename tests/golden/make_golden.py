@@ -3,11 +3,19 @@
 Runs Tsugumi's own numpy MoE forward, ReferenceModel._moe
 (Scripts/qwen35/reference_forward.py:300-334 in the reference project), on
 seeded synthetic layers from tsugumi_b200.synthetic, and stores its router
-choice and block output.  The reference project must be importable (it is
-read from TSUGUMI_REFERENCE, default /root/reference); it is only needed to
-regenerate the fixtures, never at test time.
+choice and block output.  The reference project must be importable: its
+root is read from the TSUGUMI_REFERENCE environment variable, which must be
+set (there is no default).  It is only needed to regenerate the fixtures,
+never at test time.
 
-    python tests/golden/make_golden.py
+    TSUGUMI_REFERENCE=<reference checkout> python tests/golden/make_golden.py [names...]
+
+The GeGLU fixtures run the same ``_moe`` with the module's ``silu`` replaced
+by the GeGLU activation of the reference's Swift CPU reference,
+``MoeRef.geluTanh`` (Sources/TsugumiValidation/Support/Reference/MoE/
+Moe.swift:21-29): the numpy forward is written for Qwen (SwiGLU), and this
+keeps its routing, dequantisation and combine while giving the Gemma form of
+the activation.
 
 Each fixture holds the generation parameters (config, seeds) so the tests can
 rebuild the identical inputs with numpy.
@@ -27,14 +35,30 @@ sys.path.insert(0, str(HERE.parent.parent))
 
 from tsugumi_b200.synthetic import GROUP, bf16_bits_to_f32, host_layer, host_tokens  # noqa: E402
 
-REF = Path(os.environ.get("TSUGUMI_REFERENCE", "/root/reference"))
+
+def reference_root() -> Path:
+    root = os.environ.get("TSUGUMI_REFERENCE")
+    if not root:
+        raise SystemExit("set TSUGUMI_REFERENCE to the reference project's root")
+    path = Path(root)
+    if not (path / "Scripts" / "qwen35" / "reference_forward.py").exists():
+        raise SystemExit(f"{path} does not hold Scripts/qwen35/reference_forward.py")
+    return path
 
 CASES = [
     # name, (D, F, E, K, act, shared_f), layer seed, token seed, T
     ("tiny_swiglu", (512, 256, 16, 4, 1, 0), 1234, 0, 16),
     ("tiny_shared", (512, 256, 16, 4, 1, 256), 77, 0, 16),
     ("small_qwenlike", (1024, 256, 32, 8, 1, 256), 2024, 5, 24),
+    # GeGLU (Gemma form): a small layer and the full Gemma-like shape
+    ("small_gemmalike_geglu", (1024, 256, 32, 8, 0, 0), 31, 6, 16),
+    ("gemma_geglu", (2816, 704, 128, 8, 0, 0), 4099, 9, 2),
 ]
+
+
+def gelu_tanh(x):
+    """MoeRef.geluTanh (Moe.swift:21-29), no clamp."""
+    return 0.5 * x * (1.0 + np.tanh(0.7978845608028654 * (x + 0.044715 * x * x * x)))
 
 
 def dequant(blob: np.ndarray, w_off: int, s_off: int, rows: int, cols: int) -> np.ndarray:
@@ -48,9 +72,19 @@ def dequant(blob: np.ndarray, w_off: int, s_off: int, rows: int, cols: int) -> n
 
 
 def reference_moe(layer, xn: np.ndarray):
-    sys.path.insert(0, str(REF / "Scripts" / "qwen35"))
+    sys.path.insert(0, str(reference_root() / "Scripts" / "qwen35"))
     import reference_forward as rf  # the reference's own module
 
+    rf_silu = rf.silu
+    if layer.act == 0:
+        rf.silu = gelu_tanh
+    try:
+        return _run_reference_moe(rf, layer, xn)
+    finally:
+        rf.silu = rf_silu
+
+
+def _run_reference_moe(rf, layer, xn: np.ndarray):
     d, f = layer.d, layer.f
     gw, gs, _, uw, us, _, dw, ds, _ = layer.offsets
     stride = layer.expert_stride
@@ -90,8 +124,10 @@ def reference_moe(layer, xn: np.ndarray):
     return y.astype(np.float32), dump["layer0.router_idx"], dump["layer0.router_w"]
 
 
-def main() -> None:
+def main(only: list[str]) -> None:
     for name, cfg, lseed, tseed, T in CASES:
+        if only and name not in only:
+            continue
         layer = host_layer(cfg, lseed)
         x = host_tokens(T, cfg[0], tseed)
         xf = bf16_bits_to_f32(x).astype(np.float64)
@@ -105,4 +141,4 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])  # optional fixture names: regenerate only those

@@ -143,7 +143,11 @@ def test_exact_tie_keeps_lower_index():
 # --------------------------------------------------------------------------
 # Reference forward fixtures (Scripts/qwen35/reference_forward.py:300-334)
 # --------------------------------------------------------------------------
-@pytest.mark.parametrize("name", ["tiny_swiglu", "tiny_shared", "small_qwenlike"])
+FIXTURES = ["tiny_swiglu", "tiny_shared", "small_qwenlike", "small_gemmalike_geglu",
+            "gemma_geglu"]
+
+
+@pytest.mark.parametrize("name", FIXTURES)
 def test_oracle_matches_reference_numpy_forward(name):
     fx = np.load(GOLDEN / f"{name}.npz")
     cfg = tuple(int(v) for v in fx["config"])
@@ -156,6 +160,37 @@ def test_oracle_matches_reference_numpy_forward(name):
     assert np.max(np.abs(w - fx["router_w"])) < 1e-6
     rel = np.linalg.norm(y - fx["y"]) / np.linalg.norm(fx["y"])
     assert rel < 2e-6, rel
+
+
+@pytest.mark.parametrize("name", FIXTURES)
+def test_numpy_restatement_matches_reference_numpy_forward(name):
+    """The second CPU reference (oracle/numpy_moe.py) reproduces the
+    reference's own numpy forward on every fixture, GeGLU included."""
+    from oracle import numpy_moe as NM
+
+    fx = np.load(GOLDEN / f"{name}.npz")
+    cfg = tuple(int(v) for v in fx["config"])
+    layer = host_layer(cfg, int(fx["layer_seed"]))
+    x = host_tokens(int(fx["T"]), cfg[0], int(fx["token_seed"]))
+    ids, w, _ = NM.route(layer, NM.normalise(layer, x))
+    assert np.array_equal(ids.astype(np.int32), fx["router_idx"])
+    assert np.max(np.abs(w - fx["router_w"])) < 1e-6
+    y = NM.moe_block(layer, x)
+    rel = np.linalg.norm(y - fx["y"]) / np.linalg.norm(fx["y"])
+    assert rel < 2e-6, rel
+
+
+def test_numpy_restatement_matches_oracle_on_skewed_gemma_shape():
+    """Two independent restatements agree on a Zipf-skewed GeGLU layer."""
+    from oracle import numpy_moe as NM
+
+    layer = host_layer((1024, 256, 64, 8, 0, 0), 5, skew=1.1)
+    x = host_tokens(12, 1024, 3)
+    y_c, ids_c, _ = O.OracleLayer(layer).block(x)
+    ids_n, _, _ = NM.route(layer, NM.normalise(layer, x))
+    assert np.array_equal(ids_n, ids_c)
+    y_n = NM.moe_block(layer, x)
+    assert np.linalg.norm(y_n - y_c) / np.linalg.norm(y_c) < 2e-6
 
 
 # --------------------------------------------------------------------------
