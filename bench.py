@@ -116,6 +116,15 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def host_cores() -> int:
+    """Cores this process may run on (torchrun exports OMP_NUM_THREADS=1,
+    which must not shrink the CPU baselines)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        return os.cpu_count() or 1
+
+
 def dist_env():
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
             int(os.environ.get("LOCAL_RANK", "0")))
@@ -371,6 +380,10 @@ def run_ours(args):
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline_sample(layers[:2], seconds=args.cpu_seconds)
+        try:
+            result["cpu_baseline"]["qwen_references"] = cpu_qwen_references()
+        except Exception as exc:  # reported, never hides the headline
+            result["cpu_baseline"]["qwen_references"] = {"error": repr(exc)}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
@@ -522,18 +535,55 @@ def run_ep_sweep(device, args, rank, world, local):
         f = tensors[0]["f"]
         k = tensors[0]["top_k"]
         flops = 2.0 * total * k * 3 * d * f
-        out[f"ep_prefill_{name}"] = {
+        entry = {
             "world": world, "tokens": total, "tokens_per_rank": T,
             "ms_per_layer": ms, "layer_tokens_per_s": total / (ms / 1e3),
             "routed_tflops": flops / (ms / 1e3) / 1e12,
             "path": "expert parallel (NCCL all-to-all)" if group is not None
                     else "single GPU prefill"}
+        if group is not None:
+            entry.update(ep_check_bit_equal(ctx, tensors, lays, x, world, local))
+            if getattr(lays[0], "phase_ms", None) is not None:
+                entry["phase_ms"] = lays[0].phase_ms()
+        out[f"ep_prefill_{name}"] = entry
         for lay in lays:
             lay.close()
         del lays, tensors
         torch.cuda.empty_cache()
     ctx.close()
     return out
+
+
+def ep_check_bit_equal(ctx, tensors, ep_layers, x, world, local) -> dict:
+    """After the timed expert-parallel steps: every rank recomputes its own
+    tokens through the single-GPU block (all experts resident, the same
+    tensor-core contraction: the batched GEMVs off) and compares the bits of
+    both layers' outputs.  All ranks agree on the verdict (a MAX all-reduce of
+    the mismatch flags and the largest difference)."""
+    import torch
+    import torch.distributed as dist
+    import tsugumi_b200 as tb
+
+    ctx.set_option("gemv_max_tokens", 0)
+    bad, worst = 0.0, 0.0
+    T, d = x.shape
+    for t, lay in zip(tensors, ep_layers):
+        full = tb.MoELayer(ctx, t)
+        ctx.reserve(full, T)
+        want = full.forward(x, out_dtype=torch.float32)
+        got = lay.forward(x, out_dtype=torch.float32)
+        ctx.sync()
+        if not torch.equal(got, want):
+            bad = 1.0
+        worst = max(worst, float((got - want).abs().max()))
+        full.close()
+        del want, got
+    ctx.set_option("gemv_max_tokens", 16)
+    flags = torch.tensor([bad, worst], device=x.device)
+    dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+    return {"ep_bit_equal": bool(flags[0].item() == 0.0), "ep_max_abs_diff": float(flags[1].item()),
+            "ep_check": f"each rank vs the single-GPU block on its {T} tokens, both layers, "
+                        "fp32 outputs"}
 
 
 def run_prefill_sweep(ctx, device, args):
@@ -595,6 +645,7 @@ def cpu_baseline_sample(layers, seconds: float = 12.0) -> dict:
     from oracle import oracle as O
     from tsugumi_b200.synthetic import f32_to_bf16_bits, to_host_layer
 
+    O.set_threads(host_cores())
     hosts = [O.OracleLayer(to_host_layer(l.t)) for l in layers]
     rng = np.random.default_rng(0)
     x = f32_to_bf16_bits(rng.standard_normal((1, D)).astype(np.float32))
@@ -611,6 +662,43 @@ def cpu_baseline_sample(layers, seconds: float = 12.0) -> dict:
             "sample": f"{n} layer-tokens (T=1, 2 of the 30 layers, alternating) in {dt:.1f} s"}
 
 
+def cpu_qwen_references(seconds: float = 8.0) -> dict:
+    """Both CPU references on the Qwen-like layer at T=1, on the
+    same layer and tokens: the C restatement of the Swift MoeRef (OpenMP, all
+    host cores) and the numpy restatement of the reference's numpy forward
+    ReferenceModel._moe (oracle/numpy_moe.py: the experts are dequantised for
+    every call, as the numpy forward does; BLAS threads as numpy has them)."""
+    from oracle import numpy_moe as NM
+    from oracle import oracle as O
+    from tsugumi_b200.synthetic import host_layer, host_tokens
+
+    layer = host_layer("qwen", 3)
+    x = host_tokens(1, layer.d, 11)
+    O.set_threads(host_cores())
+    ol = O.OracleLayer(layer)
+    out = {}
+    for name, fn in (("c_port", lambda: ol.block(x)), ("numpy_port", lambda: NM.moe_block(layer, x))):
+        fn()
+        n = 0
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds / 2:
+            fn()
+            n += 1
+        dt = time.perf_counter() - t0
+        out[name] = {"value": n / dt, "unit": "layer-tokens/s", "sample": f"{n} calls at T=1 in {dt:.1f} s"}
+    out["c_port"]["cores"] = O.num_threads()
+    try:
+        from threadpoolctl import threadpool_info
+        out["numpy_port"]["blas_threads"] = max(
+            (i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"),
+            default=1)
+    except Exception:  # threadpoolctl missing: report nothing rather than guess
+        out["numpy_port"]["blas_threads"] = None
+    out["kind"] = "port"
+    out["workload"] = "qwen-like MoE layer (configs[3]), decode T=1, one layer"
+    return out
+
+
 # ---------------------------------------------------------------------------
 # reference arm: the reference's CPU path (restated: the reference is Swift +
 # Metal, which has no toolchain here) on the host cores
@@ -623,6 +711,8 @@ def run_reference(args):
     from tsugumi_b200.synthetic import f32_to_bf16_bits, host_layer
 
     n_layers = 4
+    # all host cores, whatever OMP_NUM_THREADS the launcher exported
+    O.set_threads(host_cores())
     hosts = [O.OracleLayer(host_layer(CFG, 1 + 7919 * l)) for l in range(n_layers)]
     rng = np.random.default_rng(1000)
     x = f32_to_bf16_bits(rng.standard_normal((1, D)).astype(np.float32))

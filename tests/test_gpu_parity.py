@@ -119,6 +119,21 @@ def test_router_topk_matches_oracle(ctx, name, T, skew, dmax):
     assert np.max(np.abs(w16.float().cpu().numpy()[ok] - ref_w[ok])) < 1e-3
 
 
+@pytest.mark.parametrize("name,T,skew", [("gemma", 1, None), ("gemma", 200, 1.1),
+                                         ("qwen", 33, None), ("tiny", 4096, None)])
+def test_router_logits_match_oracle(ctx, name, T, skew):
+    """tsg_router_logits (encodeRouterLogitsBF16) gives the scores the oracle
+    ranks: normalised dot plus bias, fp32."""
+    host, dev, ol = layer_pair(ctx, name, 11, skew)
+    x = host_tokens(T, host.d, 300 + T)
+    out = torch.empty((T, host.num_experts), dtype=torch.float32, device="cuda")
+    tb.MoE(ctx, dev).encode_router_logits_bf16(to_dev(x), out)
+    ctx.sync()
+    _, _, _, ref = ol.router(x)
+    got = out.cpu().numpy()
+    assert np.max(np.abs(got - ref)) < 2e-6 * max(1.0, float(np.abs(ref).max()))
+
+
 def _np_pairs(rows):
     a = np.zeros((len(rows), 4), np.int32)
     for i, r in enumerate(rows):
@@ -211,8 +226,12 @@ BLOCK_CASES = [
     ("gemma", 16, None, 4, True, None),   # T > 4: grouped tcgen05 path
     ("tiny", 200, None, 4, True, None),
     ("gemma", 512, None, 4, True, 48),
-    ("gemma", 4096, 1.1, 4, True, 48),
+    # the BASELINE prefill configs: Gemma-like T=4096 with Zipf(1.1) skew
+    # (configs[2]) and Qwen-like T=4096, 512 sampled rows each
+    # plus the first and last token of the hottest expert's segment
+    ("gemma", 4096, 1.1, 4, True, 512),
     ("qwen", 1024, None, 4, True, 48),
+    ("qwen", 4096, None, 4, True, 512),
     ("gemma", 48, None, 0, True, None),
     # 4 < T <= 64: batched GEMVs (ragged token blocks, few rows per expert)
     ("tiny", 5, None, 4, True, None),
@@ -221,6 +240,17 @@ BLOCK_CASES = [
     ("qwen", 33, None, 4, True, None),
     ("qwen", 64, None, 4, True, None),
 ]
+
+
+def sample_rows(ids: np.ndarray, n: int) -> np.ndarray:
+    """n evenly spaced tokens plus the first and last token routed to the
+    most loaded expert (the two ends of its segment in the sorted pairs, so
+    the first and the last row tile of the hottest expert are checked)."""
+    T = ids.shape[0]
+    counts = np.bincount(ids.ravel(), minlength=int(ids.max()) + 1)
+    hot_tokens = np.nonzero((ids == int(np.argmax(counts))).any(axis=1))[0]
+    rows = np.linspace(0, T - 1, n).astype(int)
+    return np.unique(np.concatenate([rows, hot_tokens[:1], hot_tokens[-1:]]))
 
 
 @pytest.mark.parametrize("name,T,skew,dmax,fused,sample", BLOCK_CASES)
@@ -235,7 +265,7 @@ def test_block_forward_matches_oracle(ctx, name, T, skew, dmax, fused, sample):
     ref_ids, _, gap, _ = ol.router(x)
     ok = gap >= TIE_GAP
     assert np.array_equal(ids.cpu().numpy().astype(np.uint32)[ok], ref_ids[ok])
-    rows = np.arange(T) if sample is None else np.linspace(0, T - 1, sample).astype(int)
+    rows = np.arange(T) if sample is None else sample_rows(ids.cpu().numpy(), sample)
     y_ref, _, _ = ol.block(x[rows], ids.cpu().numpy()[rows].astype(np.uint32),
                            w.cpu().numpy()[rows])
     y_gpu = y.cpu().numpy()[rows]
