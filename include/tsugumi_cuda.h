@@ -171,6 +171,15 @@ TSG_API tsg_status tsg_router_topk(tsg_ctx ctx, tsg_moe_layer layer, const void 
                            uint32_t hidden_stride, uint32_t T, uint32_t *out_indices,
                            float *out_weights, uint16_t *out_weights_f16);
 
+/* The router's GEMV alone, with no selection behind it.  Replaces
+ * MoE.encodeRouterLogitsBF16 (MoE.swift:316-345).  out_logits [T][E] fp32
+ * (device) receives exactly the scores tsg_router_topk ranks: the dot of the
+ * layer's router row (effective scale folded in) with the hidden row, times
+ * the row's no-scale RMSNorm factor when the layer normalises its input,
+ * plus the layer's logit bias when it has one. */
+TSG_API tsg_status tsg_router_logits(tsg_ctx ctx, tsg_moe_layer layer, const void *hidden_bf16,
+                             uint32_t hidden_stride, uint32_t T, float *out_logits);
+
 /* PrefillRouter.makeTokenExpertPairs (PrefillRouter.swift:238-258), on device. */
 TSG_API tsg_status tsg_make_token_expert_pairs(tsg_ctx ctx, const uint32_t *indices,
                                        const uint16_t *weights_f16, uint32_t T, uint32_t K,
@@ -195,8 +204,9 @@ TSG_API tsg_status tsg_moe_group_pairs(tsg_ctx ctx, const tsg_token_expert_pair 
 /* No counterpart in the reference.  Same arguments, checks and outputs as
  * tsg_moe_group_pairs, but the call allocates no device memory: the
  * permutation's scratch (token-major ids and fp16 weights, the per-slot
- * occupancy flags and sorted positions, the row-tile schedule, and one
- * CTA-completion counter) lives in one fixed static device array of
+ * occupancy flags that share the sorted positions' space, the row-tile
+ * schedule and the per-chunk expert histograms)
+ * lives in one fixed static device array of
  * TSG_GROUP_NOALLOC_SCRATCH_BYTES inside this library, instead of the
  * context's workspace, which tsg_moe_group_pairs may grow with cudaMalloc.
  * It is for hosts that must not allocate from inside their enqueue path:
@@ -208,8 +218,11 @@ TSG_API tsg_status tsg_moe_group_pairs(tsg_ctx ctx, const tsg_token_expert_pair 
  * - The first call on each device resolves the array's address for that
  *   device (cudaGetSymbolAddress, with the context's device current); make
  *   that first call before recording the context's stream into anything.
- * - The completion counter must be zero when a call starts.  It is zero
- *   when the library loads and each call leaves it at zero.
+ *   After a cudaDeviceReset the next call resolves it again, so that call,
+ *   too, must come before any stream capture.
+ * - Nothing in the array has to start at zero: each call clears the
+ *   occupancy flags itself (an async memset on the stream) and writes every
+ *   other word it reads before reading it.
  * - The array is shared by every caller on a device: two calls whose work
  *   can overlap on the GPU (different streams, or different contexts of the
  *   same device, without an ordering between them) race on it and corrupt

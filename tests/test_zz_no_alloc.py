@@ -117,10 +117,15 @@ def test_noalloc_matches_existing_entry_point_on_two_calls_in_a_row(ctx, first, 
         _assert_same(out.host(a[1] * a[2]), w)
 
 
-def test_noalloc_leaves_free_device_memory_unchanged():
+@pytest.mark.parametrize("case", [
+    CASES[0],                                # multi-chunk counting sort
+    CASES[3],                                # one-CTA path (fits one chunk)
+    (200, 8, 512, 16, False, None, 5),       # one-CTA path at 512 experts
+])
+def test_noalloc_leaves_free_device_memory_unchanged(case):
     c = tb.Context(0)  # fresh context: no workspace reserved yet
     try:
-        a = _dev(CASES[0])
+        a = _dev(case)
         out = _Out(a[1] * a[2], a[3])
         _abi.check(_call(c, "tsg_moe_group_pairs_noalloc", *a, out), c.h)
         c.sync()

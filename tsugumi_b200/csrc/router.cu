@@ -584,6 +584,43 @@ __global__ void __launch_bounds__(256) router_topk_kernel(RouterParams p, RouteB
                       rb.weights_f16 ? rb.weights_f16 + static_cast<size_t>(t) * p.K : nullptr);
 }
 
+// Logits only (no selection): warp per token, the same split sum, norm factor
+// and bias as router_topk_kernel, written as fp32 [T][E].
+__global__ void __launch_bounds__(256) router_logits_kernel(RouterParams p, RouteBuffers rb,
+                                                            int ksplit, int ss_from_x,
+                                                            float* out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= p.T) return;
+  const int t = warp;
+  float ssq = 0.0f;
+  if (ss_from_x) {
+    const uint16_t* xr = p.x + static_cast<size_t>(t) * p.x_stride;
+    for (int i = lane; i < p.D; i += 32) {
+      const float v = bf16_bits_to_f32(xr[i]);
+      ssq = fmaf(v, v, ssq);
+    }
+    ssq = warp_sum(ssq);
+  } else {
+    for (int s = 0; s < ksplit; ++s) ssq += __ldcg(rb.sumsq + static_cast<size_t>(s) * p.T + t);
+  }
+  const float inv = p.norm ? rsqrtf(ssq / static_cast<float>(p.D) + p.eps) : 1.0f;
+  const float* raw = rb.logits_raw + static_cast<size_t>(t) * p.E;
+  const size_t split_stride = static_cast<size_t>(p.T) * p.E;
+  for (int e = lane; e < p.E; e += 32) {
+    float part[kMaxSplitParts];
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplitParts; ++sp)  // the order of router_topk_kernel's sum
+      part[sp] = sp < ksplit ? __ldcg(raw + sp * split_stride + e) : 0.0f;
+    float sum = 0.0f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplitParts; ++sp) sum += part[sp];
+    sum *= inv;
+    if (p.logit_bias) sum += p.logit_bias[e];
+    out[static_cast<size_t>(t) * p.E + e] = sum;
+  }
+}
+
 // Per-row statistics for caller-supplied routing: inv_rms, and for the
 // decode regime the normalised rows xn and 1.5 x their 8-element sums; the
 // raw shared-gate dot when the layer has a gate.  One CTA per token.
@@ -674,7 +711,8 @@ int router_small_ksplit(int E, int D, int* chunks_per_split) {
 }
 }  // namespace
 
-cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s) {
+cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s,
+                                  float* logits_out) {
   if (p.K > kMaxK || p.E > 512) return cudaErrorInvalidValue;
   const int mt = (p.T + kGBM - 1) / kGBM;
   const int nt = (p.E + kGBN - 1) / kGBN;
@@ -699,8 +737,11 @@ cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb,
   }
   if (e != cudaSuccess) return e;
   const int warps_per_cta = 8;
-  router_topk_kernel<<<(p.T + warps_per_cta - 1) / warps_per_cta, 256, 0, s>>>(p, rb, ksplit,
-                                                                              from_x);
+  const int grid = (p.T + warps_per_cta - 1) / warps_per_cta;
+  if (logits_out)
+    router_logits_kernel<<<grid, 256, 0, s>>>(p, rb, ksplit, from_x, logits_out);
+  else
+    router_topk_kernel<<<grid, 256, 0, s>>>(p, rb, ksplit, from_x);
   return cudaGetLastError();
 }
 

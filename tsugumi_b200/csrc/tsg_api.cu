@@ -605,10 +605,9 @@ cudaError_t grow(T** p, size_t* cap, size_t need) {
 // and cudaFree waits for the whole device, stalling every other stream the
 // host keeps busy.  tsg_moe_group_pairs may grow the context workspace with
 // both, so the no-alloc variant takes its scratch from this one array,
-// sized for TSG_GROUP_NOALLOC_MAX_PAIRS pairs and 512 experts.  Device
-// globals are zero when the module loads; the one word that must be zero
-// at the start of a call (the count kernel's CTA-completion counter) is
-// reset by the last CTA of every call.
+// sized for TSG_GROUP_NOALLOC_MAX_PAIRS pairs and 512 experts.  Every word
+// the permutation kernels read from it is written earlier in the same call,
+// so nothing in it has to start at zero.
 static __device__ __align__(256) uint8_t g_group_scratch[TSG_GROUP_NOALLOC_SCRATCH_BYTES];
 
 namespace {
@@ -623,29 +622,59 @@ constexpr size_t kGsOffW16 = kGsOffIds + gs_align(kGsPairs * 4);        // u16 [
 constexpr size_t kGsOffPos = kGsOffW16 + gs_align(kGsPairs * 2);        // u32 [P]
 constexpr size_t kGsOffTiles = kGsOffPos + gs_align(kGsPairs * 4);      // RowTile [..]
 constexpr size_t kGsOffNTiles = kGsOffTiles + gs_align(kGsRowTiles * sizeof(RowTile));
-constexpr size_t kGsOffCounter = kGsOffNTiles + 256;                    // u32, zero between calls
-constexpr size_t kGsOffHist = kGsOffCounter + 256;                      // u32 [chunks][512]
+constexpr size_t kGsOffHist = kGsOffNTiles + 256;                       // u32 [chunks][512]
 constexpr size_t kGsEnd = kGsOffHist + gs_align((kGsPairs + 2047) / 2048 * 512 * 4);
 static_assert(kGsEnd <= TSG_GROUP_NOALLOC_SCRATCH_BYTES, "group scratch layout overflows");
 
 constexpr int kGsMaxDevices = 64;
 std::mutex g_gs_mu;
 uint8_t* g_gs_addr[kGsMaxDevices] = {};
+unsigned long long g_gs_ctx_id[kGsMaxDevices] = {};
 
-// The array's address on ctx's device, resolved on the first call for that
-// device with the device current and kept for the life of the process.
+// The id of the device's current (primary) context, or 0 when the driver
+// cannot say: a cudaDeviceReset makes a new context with a new id, and the
+// module (and the array) is loaded again at another address.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&c) == CUDA_SUCCESS && c &&
+      get_id(c, &id) == CUDA_SUCCESS)
+    return id;
+  return 0;
+}
+
+// The array's address on ctx's device.  It is resolved on the first call for
+// that device, with the device current, and kept; it is resolved again when
+// the device's context has changed since (after a cudaDeviceReset).
 tsg_status group_scratch_on(tsg_ctx ctx, uint8_t** out) {
   if (ctx->device < 0 || ctx->device >= kGsMaxDevices)
     return fail(ctx, TSG_ERR_INVALID_ARG, "device ordinal out of range");
   std::lock_guard<std::mutex> lock(g_gs_mu);
-  if (!g_gs_addr[ctx->device]) {
-    TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  const unsigned long long cid = current_context_id();
+  if (!g_gs_addr[ctx->device] || cid != g_gs_ctx_id[ctx->device]) {
     void* p = nullptr;
     TSG_CUDA_TRY(ctx, cudaGetSymbolAddress(&p, g_group_scratch),
                  "cudaGetSymbolAddress(group scratch)");
     if (!p || reinterpret_cast<uintptr_t>(p) % 256 != 0)
       return fail(ctx, TSG_ERR_CUDA, "group scratch: unexpected symbol address");
     g_gs_addr[ctx->device] = static_cast<uint8_t*>(p);
+    g_gs_ctx_id[ctx->device] = cid;
   }
   *out = g_gs_addr[ctx->device];
   return TSG_OK;
@@ -840,6 +869,23 @@ tsg_status tsg_router_topk(tsg_ctx ctx, tsg_moe_layer L, const void* hidden, uin
   return TSG_OK;
 }
 
+tsg_status tsg_router_logits(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
+                             uint32_t hidden_stride, uint32_t T, float* out_logits) {
+  if (!ctx || !L) return fail(ctx, TSG_ERR_INVALID_ARG, "null context or layer");
+  if (L->ctx != ctx) return fail(ctx, TSG_ERR_INVALID_ARG, "layer belongs to another context");
+  if (T == 0) return TSG_OK;
+  if (!hidden || !out_logits) return fail(ctx, TSG_ERR_INVALID_ARG, "null buffer");
+  if (hidden_stride < L->desc.d || hidden_stride % 8)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "hidden stride is too small");
+  tsg_status st = take_pending_error(ctx);
+  if (st != TSG_OK) return st;
+  st = ensure_workspace(ctx, layer_caps(L, T));
+  if (st != TSG_OK) return st;
+  const RouterParams p = router_params(L, hidden, hidden_stride, T);
+  TSG_CUDA_TRY(ctx, launch_router_prefill(p, ctx->rb, ctx->stream, out_logits), "router logits");
+  return TSG_OK;
+}
+
 tsg_status tsg_make_token_expert_pairs(tsg_ctx ctx, const uint32_t* indices,
                                        const uint16_t* weights_f16, uint32_t T, uint32_t K,
                                        tsg_token_expert_pair* out) {
@@ -1016,7 +1062,7 @@ tsg_status tsg_moe_group_pairs_noalloc(tsg_ctx ctx, const tsg_token_expert_pair*
   rb.pair_pos = reinterpret_cast<uint32_t*>(base + kGsOffPos);
   rb.row_tiles = reinterpret_cast<RowTile*>(base + kGsOffTiles);
   rb.n_row_tiles = reinterpret_cast<uint32_t*>(base + kGsOffNTiles);
-  rb.sync_counter = reinterpret_cast<uint32_t*>(base + kGsOffCounter);
+  rb.sync_counter = nullptr;  // the permutation kernels keep no cross-CTA counter
   rb.hist = reinterpret_cast<uint32_t*>(base + kGsOffHist);
   rb.err = ctx->status;
   rb.sorted_pairs = reinterpret_cast<Pair*>(sorted_pairs);

@@ -100,8 +100,10 @@ struct RouterParams {
 // router.cu
 cudaError_t launch_router_decode(const RouterParams& p, const RouteBuffers& rb,
                                  cudaStream_t s);
+// With logits_out, writes the fp32 logits [T][E] (norm factor and bias
+// applied) instead of selecting.
 cudaError_t launch_router_prefill(const RouterParams& p, const RouteBuffers& rb,
-                                  cudaStream_t s);
+                                  cudaStream_t s, float* logits_out = nullptr);
 cudaError_t launch_rowprep(const RouterParams& p, const RouteBuffers& rb, int write_rows,
                            cudaStream_t s);
 cudaError_t launch_group_small(const RouterParams& p, const RouteBuffers& rb, cudaStream_t s);

@@ -164,6 +164,14 @@ class MoE:
                                                _ptr(out_weights), _ptr(out_weights_f16)),
               self.context.h)
 
+    def encode_router_logits_bf16(self, hidden, out_logits):
+        """encodeRouterLogitsBF16 (MoE.swift:316-345): the router's fp32
+        logits [T, E] alone, no selection."""
+        T = hidden.shape[0]
+        check(self.context.lib.tsg_router_logits(self.context.h, self.layer.h, _ptr(hidden),
+                                                 hidden.stride(0), T, _ptr(out_logits)),
+              self.context.h)
+
     def encode_routed_phases(self, x, indices, routing_weights, y, residual=None):
         """encodeRoutedPersistentPhase1U16Load + encodeRoutedPersistentPhase2Reduce
         (MoE.swift:529-644) for caller-supplied routing."""
