@@ -304,6 +304,27 @@ def test_fused_decode_graph_replay_is_stable(ctx, name, T):
     del g
 
 
+@pytest.mark.parametrize("name,T", [("tiny", 1), ("gemma", 1), ("gemma", 3), ("qwen", 1),
+                                    ("qwen", 4)])
+def test_streaming_decode_matches_earlier_fused_kernel(ctx, name, T):
+    """The streaming decode kernel (option fused_decode=1, the default) and
+    the earlier single kernel with a grid-wide act exchange (fused_decode=2)
+    give the same block output to the parity bar, and the same routing."""
+    host, dev, ol = layer_pair(ctx, name, 11, None)
+    xd = to_dev(host_tokens(T, host.d, 500 + T))
+    ys = []
+    for kind in (1, 2):
+        ctx.set_option("fused_decode", kind)
+        try:
+            ys.append(dev.forward(xd, out_dtype=torch.float32))
+            ctx.sync()
+        finally:
+            ctx.set_option("fused_decode", 1)
+    err = rel_l2(ys[0].cpu().numpy(), ys[1].cpu().numpy())
+    print(f"{name} T={T}: streaming vs earlier fused rel L2 {err:.3e}")
+    assert err < REL_L2
+
+
 @pytest.mark.parametrize("name,T", [("tiny", 7), ("gemma", 24), ("qwen", 64)])
 def test_small_batch_gemv_matches_contraction(ctx, name, T):
     """The batched GEMVs and the tensor-core contraction compute the same

@@ -68,7 +68,11 @@ struct tsg_ctx_s {
   size_t f_logits_bytes = 0;
   void* f_actfrag = nullptr;
   uint32_t* f_counters = nullptr;
+  void* f_stream = nullptr;        // streaming decode: act fragments, sums, partials
+  uint32_t* f_flags = nullptr;     // streaming decode: act flags (launch tags)
+  size_t f_flags_bytes = 0;
   bool use_fused = true;
+  int fused_kind = 1;              // 1: streaming decode kernel, 2: the earlier fused kernel
   bool allow_pdl = false;
   unsigned long long* stamps = nullptr;  // debug phase timestamps (device)
   // device status words: [0] error bits, [1] code, [2] value, [3] pad;
@@ -104,6 +108,8 @@ struct tsg_moe_layer_s {
   void* router_w3 = nullptr;     // [3][router_tc_pad(E)][D] bf16 planes of the first E rows, owned
   int has_gate = 0;
   int has_shared = 0;
+  DecodeMaps dmaps{};       // down-slice tensor maps of the streaming decode kernel
+  bool dmaps_ok = false;
 };
 
 EncodeTiledFn tsg::encode_tiled_fn() {
@@ -156,6 +162,7 @@ constexpr size_t kFusedSignalBytes = 2 * 256 * sizeof(uint32_t);
 cudaError_t reset_fused_signals(tsg_ctx ctx) {
   cudaError_t e = cudaMemset(ctx->f_counters, 0, kFusedSignalBytes);
   if (e == cudaSuccess && ctx->f_logits) e = cudaMemset(ctx->f_logits, 0, ctx->f_logits_bytes);
+  if (e == cudaSuccess && ctx->f_flags) e = cudaMemset(ctx->f_flags, 0, ctx->f_flags_bytes);
   return e;
 }
 
@@ -207,7 +214,17 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
   void* f_logits = take(4 * Tf * (E + 1) * 8);
   void* f_actfrag = take(rows_f * F * 2);
   uint32_t* f_counters = static_cast<uint32_t*>(take(kFusedSignalBytes));
+  // streaming decode: data scratch and act flags
+  const size_t fs_bytes = decode_stream_scratch_bytes(static_cast<int>(Tf), static_cast<int>(D),
+                                                      static_cast<int>(F), static_cast<int>(K));
+  const size_t ff_bytes =
+      decode_stream_flag_bytes(static_cast<int>(Tf), static_cast<int>(F), static_cast<int>(K));
+  void* f_stream = take(fs_bytes);
+  uint32_t* f_flags = static_cast<uint32_t*>(take(ff_bytes));
   if (base) {
+    ctx->f_stream = f_stream;
+    ctx->f_flags = f_flags;
+    ctx->f_flags_bytes = ff_bytes;
     ctx->f_logits = f_logits;
     ctx->f_logits_bytes = 4 * Tf * (E + 1) * 8;
     ctx->f_actfrag = f_actfrag;
@@ -354,6 +371,8 @@ tsg_status run_decode_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, ui
   return TSG_OK;
 }
 
+bool stream_ok(tsg_ctx ctx, const tsg_moe_layer_s* L, uint32_t T);
+
 tsg_status run_decode_fused(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
                             uint32_t T, const uint32_t* ids_in, const float* w_in,
                             const float* residual, void* y, uint32_t y_stride, tsg_dtype y_dtype,
@@ -393,7 +412,12 @@ tsg_status run_decode_fused(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint
   a.num_sms = ctx->num_sms;
   a.allow_pdl = ctx->allow_pdl ? 1 : 0;
   a.stamps = ctx->stamps;
-  TSG_CUDA_TRY(ctx, launch_decode_fused(a, ctx->stream), "fused decode");
+  if (stream_ok(ctx, L, T)) {
+    TSG_CUDA_TRY(ctx, launch_decode_stream(a, L->dmaps, ctx->f_stream, ctx->f_flags, ctx->stream),
+                 "streaming decode");
+  } else {
+    TSG_CUDA_TRY(ctx, launch_decode_fused(a, ctx->stream), "fused decode");
+  }
   prof_mark(ctx, 1);
   prof_mark(ctx, 2);
   prof_mark(ctx, 3);
@@ -401,7 +425,18 @@ tsg_status run_decode_fused(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint
   return TSG_OK;
 }
 
+// The streaming decode kernel takes the batch when it is selected (the
+// default) and the shape is one it supports.
+bool stream_ok(tsg_ctx ctx, const tsg_moe_layer_s* L, uint32_t T) {
+  return ctx->use_fused && ctx->fused_kind == 1 && L->dmaps_ok &&
+         decode_stream_supported(static_cast<int>(T), static_cast<int>(L->desc.d),
+                                 static_cast<int>(L->desc.f), static_cast<int>(L->desc.top_k),
+                                 static_cast<int>(L->desc.num_experts), L->has_gate,
+                                 L->has_shared, ctx->num_sms);
+}
+
 bool fused_ok(tsg_ctx ctx, const tsg_moe_layer_s* L, uint32_t T) {
+  if (stream_ok(ctx, L, T)) return true;
   return ctx->use_fused &&
          decode_fused_supported(static_cast<int>(T), static_cast<int>(L->desc.top_k),
                                 static_cast<int>(L->desc.num_experts), L->has_gate, ctx->num_sms) &&
@@ -739,7 +774,12 @@ tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t) {
 tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char* name, int64_t value) {
   if (!ctx || !name) return fail(ctx, TSG_ERR_INVALID_ARG, "null argument");
   const std::string n(name);
-  if (n == "fused_decode") ctx->use_fused = value != 0;
+  if (n == "fused_decode") {
+    // 0: router / gate-up / down kernels; 1: the streaming single kernel
+    // (default); 2: the earlier single kernel with a grid-wide act exchange
+    ctx->use_fused = value != 0;
+    ctx->fused_kind = value == 2 ? 2 : 1;
+  }
   else if (n == "programmatic_launch") ctx->allow_pdl = value != 0;
   else if (n == "gemv_max_tokens") ctx->gemv_max_tokens = static_cast<uint32_t>(value < 0 ? 0 : value);
   else if (n == "debug_phase_stamps")
@@ -826,6 +866,10 @@ tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc* d, tsg_mo
       e = launch_split_router(L->router_rows, static_cast<int>(d->num_experts),
                               static_cast<int>(d->d), L->router_w3, ctx->stream);
   }
+  if (e == cudaSuccess)
+    L->dmaps_ok = encode_decode_maps(expert_set(L), static_cast<int>(d->d),
+                                     static_cast<int>(d->f), static_cast<int>(d->num_experts),
+                                     &L->dmaps);
   if (e != cudaSuccess) {
     if (L->router_rows) cudaFree(L->router_rows);
     if (L->router_w3) cudaFree(L->router_w3);

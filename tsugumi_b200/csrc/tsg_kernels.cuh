@@ -178,6 +178,25 @@ struct DecodeFusedArgs {
   int allow_pdl;
   unsigned long long* stamps;  // debug phase timestamps [grid][8], or nullptr
 };
+// decode_stream.cu: the same block, streaming every selected weight byte in
+// one phase.  Its down slices arrive by TMA; the maps are encoded once per
+// layer (routed experts, and the shared expert when there is one).
+struct DecodeMaps {
+  CUtensorMap down128, down16;    // routed down codes: [E][D][F/2], 32-byte x 128 / 16 rows
+  CUtensorMap sdown128, sdown16;  // the shared expert's [D][F/2]
+  CUtensorMap gate8, up8;         // routed gate / up codes: 8 rows x D/2 bytes, 128-byte swizzle
+  CUtensorMap sgate8, sup8;       // the shared expert's
+};
+bool encode_decode_maps(const ExpertSet& ex, int D, int F, int E, DecodeMaps* out);
+bool decode_stream_supported(int T, int D, int F, int K, int E, int has_gate, int has_shared,
+                             int num_sms);
+// workspace of decode_stream (bytes) for at most T tokens: partial sums,
+// and the tagged act words (zero at allocation and after an error)
+size_t decode_stream_scratch_bytes(int T, int D, int F, int K);
+size_t decode_stream_flag_bytes(int T, int F, int K);
+cudaError_t launch_decode_stream(const DecodeFusedArgs& a, const DecodeMaps& maps,
+                                 void* scratch, void* acts, cudaStream_t s);
+
 bool decode_fused_supported(int T, int K, int E, int has_gate, int num_sms);
 bool decode_fused_fits(int T, int D, int F, int K, int has_shared, int num_sms);
 cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t s);
