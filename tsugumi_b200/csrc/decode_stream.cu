@@ -72,6 +72,7 @@ constexpr int kLogitCopies = 4;
 constexpr int kStamps = 32;
 constexpr int kDownBox = 128;    // rows of the large down box (8 blocks of 16)
 constexpr float kTwo20 = 1048576.0f;
+constexpr int kParts = 3;  // rows owned: each down tile's K split over three work units
 
 // Cross-CTA signalling (same scheme as the earlier fused decode kernel):
 // per-CTA launch epochs, the grid counter of each launch parity.
@@ -101,6 +102,7 @@ struct StreamParams {
   unsigned long long* tlogits;  // [kLogitCopies][T][E + 1] (tag << 32 | bits)
   float* inv_rms;               // [T]
   unsigned long long* hact;     // [slots][T][F / 8][4] act fragments, (tag << 32 | half2) words
+  uint32_t* gdone;              // [grid] launch tag once a CTA's acts are all published
   float* partial;               // [slots][F / 64][T][D] down partial sums (x 2^-20)
   uint32_t* counters;           // Signals
   uint32_t* ids_out;            // [T][K]
@@ -127,16 +129,24 @@ struct Plan {
   uint32_t sb;         // stage bytes
   uint32_t sd;         // down blocks (16 rows) per down stage
   uint32_t red_words;  // floats one warp leaves per gate/up block
+  // T <= 2 ("rows of y owned"): the acts of every slot, their accumulator
+  // starts, and the CTA's down results, all in shared memory
+  uint32_t act_off;    // [slots][T][F / 8] uint4 act fragments
+  uint32_t ast_off;    // [slots][F / 32][T] float accumulator starts
+  uint32_t sv_off;     // [slots][T][16 nt] float down results of the CTA's rows
   uint32_t total;      // bytes of the whole plan for `ring` stages
 };
+
+// Whether the CTAs own rows of y (T <= 2: every slot's acts fit in shared
+// memory, so a CTA computes whole down rows and combines them itself).
+__host__ __device__ inline bool rows_owned(int T) { return T <= 2; }
 
 __host__ __device__ inline uint32_t red_words_for(int T) {
   // lanes with c < ceil(T / 2) hold the valid columns; T = 1 keeps d0 and d2
   return T == 1 ? 16u : (T == 2 ? 32u : 64u);
 }
 
-__host__ __device__ inline Plan make_plan(int T, int D, int F, int ring) {
-  (void)F;
+__host__ __device__ inline Plan make_plan(int T, int D, int F, int K, int G, int ring) {
   Plan L;
   uint32_t o = 0;
   L.xf_off = o;
@@ -147,6 +157,18 @@ __host__ __device__ inline Plan make_plan(int T, int D, int F, int ring) {
   L.red_off = o;
   L.red_words = red_words_for(T);
   o += static_cast<uint32_t>(ring) * kWarps * L.red_words * 4u;
+  L.act_off = L.ast_off = L.sv_off = o;
+  if (rows_owned(T)) {
+    const uint32_t slots = static_cast<uint32_t>(T * K + 1);
+    const uint32_t ntmax = static_cast<uint32_t>((D / 16 + G - 1) / G);
+    o = align_up_u32(o, 16);
+    L.act_off = o;
+    o += slots * static_cast<uint32_t>(T * (F / 8)) * 16u;
+    L.ast_off = o;
+    o += slots * static_cast<uint32_t>((F / 32) * T) * 4u;
+    L.sv_off = o;
+    o += kParts * slots * static_cast<uint32_t>(T) * 16u * ntmax * 4u;
+  }
   L.ring_off = align_up_u32(o, 1024);
   L.rs = static_cast<uint32_t>(4 * D);  // bytes of one 8-row code box
   const uint32_t gu = 2u * L.rs + 2u * 8u * static_cast<uint32_t>(D / 16);
@@ -159,6 +181,8 @@ __host__ __device__ inline Plan make_plan(int T, int D, int F, int ring) {
 
 // Stage descriptor: kind (0 gate/up block, 1 down blocks), slot, chunk, and
 // the gate/up block in the chunk or the first down block and their count.
+// With rows owned, a down stage is `chunk` consecutive slots from `slot`,
+// each with the down rows of 16-row tiles [a, a + n) of y.
 struct Stage {
   uint16_t kind_slot;  // kind << 8 | slot
   uint16_t chunk;
@@ -176,13 +200,22 @@ TSG_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, ui
 }
 
 // mma.sync m16n8k16 fp16 x fp16 + C -> fp32, with a separate C operand.
+// Not volatile: the MMAs have no side effects, so the compiler may interleave
+// independent accumulation chains instead of issuing each dependent pair
+// back to back.
 TSG_DEV void mma_16816_c(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                          uint32_t b0, uint32_t b1, float c0, float c1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%10,%11};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1));
+}
+TSG_DEV void mma_16816_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                           uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // The four unscaled fp16 pairs of a code word (see the file header):
@@ -205,7 +238,7 @@ TSG_DEV void mma_group(float (&d)[4], uint32_t ra, uint32_t rb, const uint4& bx,
   split_word(ra, pa);
   split_word(rb, pb);
   mma_16816_c(d, pa[0], pb[0], pa[1], pb[1], bx.x, bx.y, c0, c1);
-  mma_16816(d, pa[2], pb[2], pa[3], pb[3], bx.z, bx.w);
+  mma_16816_acc(d, pa[2], pb[2], pa[3], pb[3], bx.z, bx.w);
 }
 
 // Eight consecutive values as the operand chunk of the unscaled scheme:
@@ -235,6 +268,14 @@ TSG_DEV unsigned long long ld_relaxed_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+TSG_DEV uint32_t ld_relaxed_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+TSG_DEV void st_relaxed_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 TSG_DEV uint32_t ld_acquire_u32(const uint32_t* p) {
   uint32_t v;
@@ -305,10 +346,15 @@ TSG_DEV float key_value(uint32_t k) {
 struct Work {
   uint32_t nslots, nc, nd;  // slots, 64-f chunks per slot, 16-row blocks per chunk
   uint32_t ng, ndt;         // gate/up blocks, down blocks of the layer
+  bool rows_owned;          // T <= 2: phase 2 is whole rows of y per CTA
+  uint32_t sb, tile_bytes;  // stage bytes; one slot's 16 down rows (codes + scales)
 };
 
-TSG_DEV Work make_work(int nslots, int D, int F) {
+TSG_DEV Work make_work(int nslots, int D, int F, int T, uint32_t sb) {
   Work w;
+  w.rows_owned = rows_owned(T);
+  w.sb = sb;
+  w.tile_bytes = 16u * static_cast<uint32_t>(F / 2 + F / 16);
   w.nslots = static_cast<uint32_t>(nslots);
   w.nc = static_cast<uint32_t>(F / 64);
   w.nd = static_cast<uint32_t>(D / 16);
@@ -332,6 +378,23 @@ TSG_DEV int build_stages(const Work& w, int bid, int G, uint32_t sd, Stage* st) 
     st[n].a = static_cast<uint16_t>(rb & 7u);
     st[n].n = 1;
     ++n;
+  }
+  if (w.rows_owned) {
+    // the CTA's 16-row tiles of y [t0, t1), every slot's down rows of them,
+    // as many slots per stage as fit
+    const uint32_t t0 = (w.nd * ub) / ug, t1 = (w.nd * (ub + 1)) / ug, nt = t1 - t0;
+    if (nt == 0) return n;
+    uint32_t per = w.sb / (nt * w.tile_bytes);
+    if (per > 32u) per = 32u;  // one issuing lane per slot
+    for (uint32_t slot = 0; slot < w.nslots; slot += per) {
+      if (n >= kMaxStages || per == 0) return -1;
+      st[n].kind_slot = static_cast<uint16_t>((1u << 8) | slot);
+      st[n].chunk = static_cast<uint16_t>(w.nslots - slot < per ? w.nslots - slot : per);
+      st[n].a = static_cast<uint16_t>(t0);
+      st[n].n = static_cast<uint16_t>(nt);
+      ++n;
+    }
+    return n;
   }
   const uint32_t d0 = (w.ndt * ub) / ug, d1 = (w.ndt * (ub + 1)) / ug;
   for (uint32_t k = d0; k < d1;) {
@@ -384,7 +447,7 @@ TSG_DEV void tma_load_4d_bar(uint32_t dst, const CUtensorMap* map, uint64_t* bar
 // compute its blocks load them directly.
 TSG_DEV void issue_stage(const StreamParams& p, const Plan& L, const Stage& sg, const int* slot_expert,
                          uint8_t* dst, uint64_t* bar, int lane) {
-  const int D = p.D;
+  const int D = p.D, F = p.F;
   const int slot = sg.kind_slot & 0xFF;
   const bool down = (sg.kind_slot >> 8) != 0;
   const int e = slot_expert[slot];
@@ -403,6 +466,23 @@ TSG_DEV void issue_stage(const StreamParams& p, const Plan& L, const Stage& sg, 
                 8u * sbytes, bar);
       bulk_load(dst + 2u * L.rs + 8u * sbytes, blob + off->up_s + static_cast<size_t>(f0) * sbytes,
                 8u * sbytes, bar);
+    }
+  } else if (rows_owned(p.T)) {
+    // `chunk` slots, each: down codes of rows [16 a, 16 (a + n)) (contiguous),
+    // then their scales (contiguous)
+    const int nsl = sg.chunk, nt = sg.n;
+    const uint32_t cb = 16u * nt * static_cast<uint32_t>(F / 2);
+    const uint32_t sbytes = 16u * nt * static_cast<uint32_t>(F / 16);
+    if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nsl) * (cb + sbytes));
+    __syncwarp();
+    if (lane < nsl) {
+      const ExpertOffsets* o2;
+      const uint8_t* b2 = slot_blob(p, slot_expert[slot + lane], &o2);
+      const size_t r0 = 16u * static_cast<size_t>(sg.a);
+      bulk_load(dst + static_cast<uint32_t>(lane) * (cb + sbytes), b2 + o2->down_w + r0 * (F / 2), cb,
+                bar);
+      bulk_load(dst + static_cast<uint32_t>(lane) * (cb + sbytes) + cb,
+                b2 + o2->down_s + r0 * (F / 16), sbytes, bar);
     }
   } else {
     const int n = sg.n, nbig = n / 8;
@@ -434,6 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t bar_rw;
   __shared__ __align__(8) uint64_t bar_st[kMaxRing];
   __shared__ __align__(8) uint64_t bar_rel[kMaxRing];
+  __shared__ __align__(8) uint64_t bar_act, bar_act2;  // compute warps, once per launch
+  __shared__ __align__(8) uint64_t bar_go;              // warp 0: every CTA's acts are out
   __shared__ int s_issued[kMaxRing];
   __shared__ Stage s_stage[kMaxStages];
   __shared__ int s_ids[kMaxTok][kMaxK];
@@ -461,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool fast1 = TT == 1 && p.ids_in == nullptr;
   Signals* sig = reinterpret_cast<Signals*>(p.counters);
   uint32_t* err = p.err;
-  const Plan L = make_plan(T, D, F, NS);
+  const Plan L = make_plan(T, D, F, K, G, NS);
   uint4* xf = reinterpret_cast<uint4*>(smem + L.xf_off);
   float* cinit = reinterpret_cast<float*>(smem + L.ci_off);
   float* red = reinterpret_cast<float*>(smem + L.red_off);
@@ -482,6 +564,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_issued[tid - 32] = 0;
   }
   if (tid == 64) s_epoch = __ldcg(&sig->epoch[bid]) + 1u;  // this launch's tag
+  if (tid == 96) {
+    mbar_init(&bar_act, kWarps);
+    mbar_init(&bar_act2, kWarps);
+    mbar_init(&bar_go, 1);
+    fence_mbar_init();
+  }
   if (tid == 0) {
     mbar_init(&bar_rw, 1);
     fence_mbar_init();
@@ -668,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (fast1 && warp == kWarps && lane == 0) {
     // the share of one token's layer does not depend on the input: plan it
     // while warp 0 waits for the logits
-    const int n = build_stages(make_work(K + p.has_shared, D, F), bid, G, L.sd, s_stage);
+    const int n = build_stages(make_work(K + p.has_shared, D, F, T, L.sb), bid, G, L.sd, s_stage);
     s_nst = n;
     if (n < 0) flag_error(err, TSG_DEVERR_BOUNDS);  // the host's shape checks rule this out
   }
@@ -826,7 +914,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (nslots < 0) return;  // invalid caller routing: nothing in flight
   if (!fast1) {
     if (tid == 0) {
-      const int n = build_stages(make_work(nslots, D, F), bid, G, L.sd, s_stage);
+      const int n = build_stages(make_work(nslots, D, F, T, L.sb), bid, G, L.sd, s_stage);
       s_nst = n;
       if (n < 0) flag_error(err, TSG_DEVERR_BOUNDS);  // the host's shape checks rule this out
     }
@@ -868,6 +956,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int m = lane >> 3, r8 = lane & 7;
   bool failed = false;
+  const int GF = F / 32;
+  uint4* afr = reinterpret_cast<uint4*>(smem + L.act_off);
+  float* ast = reinterpret_cast<float*>(smem + L.ast_off);
+  float* sv = reinterpret_cast<float*>(smem + L.sv_off);
   // acts of the last (slot, chunk) a down stage used, kept for the next one
   int act_key = -1;
   uint4 ba[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
@@ -930,6 +1022,179 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c < 2)
           *reinterpret_cast<float4*>(mine + 4 * (2 * g + c)) = make_float4(acc[0], acc[1], acc[2], acc[3]);
       }
+    } else if (rows_owned(T)) {
+      // ---- (reached once, at the first down stage) ----
+      // every slot's acts into shared memory: warp 0 first waits until every
+      // CTA has flagged its gate/up blocks published, so that the tagged
+      // words are read about once instead of polled by every thread (the tags
+      // stay the proof: a word that is not there yet is read again)
+      if (warp == 0) {
+        const unsigned long long t0 = global_timer_ns();
+        for (uint32_t spin = 0;; ++spin) {
+          bool all = true;
+          for (int i = lane; i < G; i += 32) all &= ld_relaxed_u32(p.gdone + i) == tag;
+          if (__all_sync(0xFFFFFFFFu, all)) break;
+          if ((spin & 15u) == 15u &&
+              __any_sync(0xFFFFFFFFu, lane == 0 && poll_give_up(t0, err))) {
+            failed = true;
+            break;
+          }
+          __nanosleep(100);
+        }
+        if (lane == 0) mbar_arrive(&bar_go);
+      }
+      if (failed || !__all_sync(0xFFFFFFFFu, mbar_wait_inl(&bar_go, 0, err))) {
+        failed = true;
+        break;
+      }
+      stamp(9);  // debug: every CTA's acts seen out
+      // the tagged words, coalesced (one word per lane, eight in flight per
+      // thread), then the accumulator start of each (slot, token, group):
+      // -8 * 2^-20 * sum of its 32 acts
+      {
+        const int nw = nslots * T * F8 * 4;
+        uint32_t* a32 = reinterpret_cast<uint32_t*>(afr);
+        const int ct = warp * 32 + lane;
+        for (int w0 = ct; w0 < nw && !failed; w0 += 8 * kWarps * 32) {
+          unsigned long long wv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int w = w0 + u * kWarps * 32;
+            wv[u] = w < nw ? ld_relaxed_u64(p.hact + w) : (static_cast<unsigned long long>(tag) << 32);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int w = w0 + u * kWarps * 32;
+            if (w >= nw) continue;
+            const unsigned long long t0 = global_timer_ns();
+            for (uint32_t spin = 0; static_cast<uint32_t>(wv[u] >> 32) != tag; ++spin) {
+              if ((spin & 15u) == 15u && poll_give_up(t0, err)) {
+                failed = true;
+                break;
+              }
+              __nanosleep(128);
+              wv[u] = ld_relaxed_u64(p.hact + w);
+            }
+            a32[w] = static_cast<uint32_t>(wv[u]);
+          }
+        }
+      }
+      failed = __any_sync(0xFFFFFFFFu, failed);
+      if (failed) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_act);
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait_inl(&bar_act, 0, err))) {
+        failed = true;
+        break;
+      }
+      {
+        const int na = nslots * T * GF;
+        for (int q = warp * 32 + lane; q < na; q += kWarps * 32) {
+          const int st_ = q / GF, grp = q - st_ * GF;  // st_ = slot * T + t
+          const uint4* fr = afr + static_cast<size_t>(st_) * F8 + 4 * grp;
+          float sm = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 u = fr[i];
+            const float2 h0 = h2_to_f2(u.x), h1 = h2_to_f2(u.y);
+            const float2 h2 = h2_to_f2(u.z), h3 = h2_to_f2(u.w);
+            sm += ((h0.x + h0.y) + (h1.x + h1.y)) * 0.0625f + ((h2.x + h2.y) + (h3.x + h3.y));
+          }
+          const int sl = st_ / T, t = st_ - sl * T;
+          ast[(static_cast<size_t>(sl) * GF + grp) * T + t] = -8.0f / kTwo20 * sm;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_act2);
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait_inl(&bar_act2, 0, err))) {
+        failed = true;
+        break;
+      }
+      stamp(22);  // debug: acts loaded
+      // ---- down work units: (slot k of a stage, 16-row tile j, part kp of
+      // the K = F pairs); with every down stage resident in the ring at once
+      // (the host checks it), the units of all of them are spread over the
+      // warps together; else stage by stage ----
+      const int NP2 = F / 64;
+      const bool together = (nst - s) <= NS;
+      int ubase = 0;
+      int dbg_units = 0;
+      for (int s2 = s; s2 < nst && !failed; ++s2) {
+        const Stage sg2 = s_stage[s2];
+        const int rs2 = s2 % NS;
+        const uint8_t* base2 = ring + static_cast<uint32_t>(rs2) * L.sb;
+        const uint32_t par2 = static_cast<uint32_t>(s2 / NS) & 1u;
+        const int slot2 = sg2.kind_slot & 0xFF;
+        const int nsl = sg2.chunk, nt = sg2.n, RWS = 16 * nt;
+        const int nunits = nsl * nt * kParts;
+        const uint32_t cb = 16u * nt * static_cast<uint32_t>(F / 2);
+        const uint32_t sbb = cb + 16u * nt * static_cast<uint32_t>(F / 16);
+        int first = together ? ((warp - ubase) % kWarps + kWarps) % kWarps : warp;
+        if (first < nunits &&
+            !__all_sync(0xFFFFFFFFu, mbar_wait_inl(&bar_st[rs2], par2, err))) {
+          failed = true;
+          break;
+        }
+        if (s2 == s) stamp(21);  // debug: warp 0 starts its down units
+        for (int u = first; u < nunits; u += kWarps) {
+          const int item = u / kParts, kp = u - item * kParts;
+          const int k = item / nt, j = item - k * nt, sl = slot2 + k;
+          const int p0 = (kp * NP2) / kParts, p1 = ((kp + 1) * NP2) / kParts;
+          const uint32_t rowaddr = smem_u32(base2) + static_cast<uint32_t>(k) * sbb +
+                                   static_cast<uint32_t>(16 * j + r8 + 8 * (m & 1)) * (F / 2) +
+                                   static_cast<uint32_t>(m >> 1) * 16u;
+          const __half* scs =
+              reinterpret_cast<const __half*>(base2 + static_cast<uint32_t>(k) * sbb + cb) + 16 * j * GF;
+          const uint4* af = afr + (static_cast<size_t>(sl) * T + (g < T ? g : 0)) * F8 + c;
+          const float* as = ast + static_cast<size_t>(sl) * GF * T;
+          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+          for (int pr = p0; pr < p1; ++pr) {
+            uint32_t q0, q1, q2, q3;
+            ldsm_x4(rowaddr + static_cast<uint32_t>(pr) * 32u, q0, q1, q2, q3);
+            const uint4 b0 = g < T ? af[8 * pr] : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 b1 = g < T ? af[8 * pr + 4] : make_uint4(0u, 0u, 0u, 0u);
+            const float c00 = 2 * c < T ? as[(2 * pr) * T + 2 * c] : 0.0f;
+            const float c01 = 2 * c + 1 < T ? as[(2 * pr) * T + 2 * c + 1] : 0.0f;
+            const float c10 = 2 * c < T ? as[(2 * pr + 1) * T + 2 * c] : 0.0f;
+            const float c11 = 2 * c + 1 < T ? as[(2 * pr + 1) * T + 2 * c + 1] : 0.0f;
+            float d0[4], d1[4];
+            mma_group(d0, q0, q1, b0, c00, c01);
+            mma_group(d1, q2, q3, b1, c10, c11);
+            const float2 sr = h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + g * GF + 2 * pr));
+            const float2 sh =
+                h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + (g + 8) * GF + 2 * pr));
+            acc[0] = fmaf(sr.y, d1[0], fmaf(sr.x, d0[0], acc[0]));
+            acc[1] = fmaf(sr.y, d1[1], fmaf(sr.x, d0[1], acc[1]));
+            acc[2] = fmaf(sh.y, d1[2], fmaf(sh.x, d0[2], acc[2]));
+            acc[3] = fmaf(sh.y, d1[3], fmaf(sh.x, d0[3], acc[3]));
+          }
+          float* svs = sv + (static_cast<size_t>(kp) * nslots + sl) * T * RWS + 16 * j;
+          if (2 * c < T) {
+            svs[(2 * c) * RWS + g] = acc[0];
+            svs[(2 * c) * RWS + g + 8] = acc[2];
+          }
+          if (2 * c + 1 < T) {
+            svs[(2 * c + 1) * RWS + g] = acc[1];
+            svs[(2 * c + 1) * RWS + g + 8] = acc[3];
+          }
+          if (dbg_units < 2) stamp(19 + dbg_units);  // debug: warp 0's first units
+          ++dbg_units;
+        }
+        ubase += nunits;
+        if (!together) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_rel[rs2]);
+        }
+      }
+      if (failed) break;
+      stamp(23);  // debug: warp 0's down units done
+      if (together)
+        for (int s2 = s; s2 < nst; ++s2) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_rel[s2 % NS]);
+        }
+      break;  // every remaining stage is done and released
     } else {
       // this warp's blocks of the stage: k = warp + 15 j (at most 3); their
       // down scales (groups 2 ch, 2 ch + 1 of rows g and g + 8) are loaded
@@ -1029,7 +1294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (s < 12) stamp(12 + s);  // debug: warp 0 done with stage s
+    if (s < 7) stamp(12 + s);  // debug: warp 0 done with stage s
     // release the stage to the reduction warp (which refills its ring slot)
     __syncwarp();
     if (lane == 0) mbar_arrive(&bar_rel[rs]);
@@ -1038,6 +1303,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the reduction and refill warp: for every stage, once all compute warps
     // have released it, reduce a gate/up block's partials (in warp order),
     // publish its acts, and request the stage that reuses the ring slot
+    // (gate/up stages come first; once the last is published, this CTA
+    // flags its acts as out)
+    int ngu = 0;
+    while (ngu < nst && (s_stage[ngu].kind_slot >> 8) == 0) ++ngu;
+    if (ngu == 0 && lane == 0) {
+      st_relaxed_u32(p.gdone + bid, tag);
+      __threadfence();
+    }
     for (int s = 0; s < nst && !failed; ++s) {
       const Stage sg = s_stage[s];
       const int rs = s % NS;
@@ -1098,6 +1371,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       }
+      if (s == ngu - 1) {
+        // the block's act words, then the flag: a fence on each side, so that
+        // both leave this SM now rather than whenever its store queue drains
+        // (once per CTA, on this warp only)
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) {
+          st_relaxed_u32(p.gdone + bid, tag);
+          __threadfence();
+          if (p.stamps) stamp_at(p.stamps, bid * kStamps + 11);  // debug: acts out
+        }
+        __syncwarp();
+      }
       if (s + NS < nst) {
         issue_stage(p, L, s_stage[s + NS], s_slot_expert, base, &bar_st[rs], lane);
         if (lane == 0) ++s_issued[rs];
@@ -1114,6 +1400,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0)
       for (int i = 0; i < NS; ++i)
         if (s_issued[i] > 0) drain_wait(&bar_st[i], static_cast<uint32_t>(s_issued[i] - 1) & 1u);
+    return;
+  }
+
+  if (rows_owned(T)) {
+    // ---------------- this CTA's rows of y, combined here ----------------
+    // y = residual + gate * shared + sum over ranks (ascending) w * v.  No
+    // grid counter is used; the next launch's counter is still cleared, as
+    // every launch that passes its grid barrier does, since the next launch
+    // may be one of the kernels that counts on it starting at zero.
+    if (bid == 0 && tid == 0) sig->gcount[(tag & 1u) ^ 1u] = 0u;
+    const uint32_t ntl = static_cast<uint32_t>(D / 16);
+    const int t0 = static_cast<int>((ntl * static_cast<uint32_t>(bid)) / static_cast<uint32_t>(G));
+    const int t1 = static_cast<int>((ntl * static_cast<uint32_t>(bid + 1)) / static_cast<uint32_t>(G));
+    const int RWS = 16 * (t1 - t0);
+    // v of (slot, token, row): its K parts added in order, in place of part 0
+    for (int q = tid; q < nslots * T * RWS; q += kThreads) {
+      float v = 0.0f;
+#pragma unroll
+      for (int kp = 0; kp < kParts; ++kp) v += sv[static_cast<size_t>(kp) * nslots * T * RWS + q];
+      sv[q] = v * kTwo20;
+    }
+    __syncthreads();
+    auto vsum = [&](int sl, int t, int rl) {
+      return sv[(static_cast<size_t>(sl) * T + t) * RWS + rl];
+    };
+    for (int q = tid; q < T * RWS; q += kThreads) {
+      const int t = q / RWS, rl = q - t * RWS, d = 16 * t0 + rl;
+      float y = p.residual ? p.residual[static_cast<size_t>(t) * D + d] : 0.0f;
+      if (p.has_shared) {
+        const float v = vsum(nslots - 1, t, rl);
+        y = p.has_gate ? fmaf(s_gate[t], v, y) : y + v;
+      }
+      for (int r = 0; r < K; ++r) {
+        const int sl = fast1 ? r : s_pos_slot[s_pair_pos[t * K + r]];
+        y = fmaf(s_w[t][r], vsum(sl, t, rl), y);
+      }
+      if (p.y_f32)
+        reinterpret_cast<float*>(p.y)[static_cast<size_t>(t) * p.y_stride + d] = y;
+      else
+        reinterpret_cast<__nv_bfloat16*>(p.y)[static_cast<size_t>(t) * p.y_stride + d] =
+            __float2bfloat16_rn(y);
+    }
+    stamp(7);
+    if (tid == 0) sig->epoch[bid] = tag;  // read by this CTA's next launch
     return;
   }
 
@@ -1204,18 +1534,27 @@ size_t stream_smem_limit() {
 }
 
 // Ring stages for this shape within the shared memory limit (0: does not fit).
-int ring_slots_for(int T, int D, int F) {
+int ring_slots_for(int T, int D, int F, int K, int G) {
   const size_t lim = stream_smem_limit();
   for (int ns = kMaxRing; ns >= 2; --ns)
-    if (make_plan(T, D, F, ns).total <= lim) return ns;
+    if (make_plan(T, D, F, K, G, ns).total <= lim) return ns;
   return 0;
 }
 
 // An upper bound of the stages of one CTA's share (largest slot count).
-long long max_stages_bound(int T, int D, int F, int K, int E, int has_shared, int G, uint32_t sd) {
+long long max_stages_bound(int T, int D, int F, int K, int E, int has_shared, int G, uint32_t sd,
+                           uint32_t sb) {
   const long long nslots = std::min(T * K, E) + (has_shared ? 1 : 0);
   const long long ng = nslots * (F / 8), nd = D / 16, ndt = nslots * (F / 64) * nd;
   const long long gshare = (ng + G - 1) / G, dshare = (ndt + G - 1) / G;
+  if (rows_owned(T)) {
+    // whole down rows of every slot, packed slots per stage
+    const long long ntmax = (nd + G - 1) / G;
+    const long long sbb = ntmax * 16 * (F / 2 + F / 16);
+    const long long per = sbb > 0 ? std::min<long long>(32, static_cast<long long>(sb) / sbb) : 1;
+    if (per < 1) return kMaxStages + 1;
+    return gshare + 1 + (nslots + per - 1) / per;
+  }
   return gshare + dshare / sd + dshare / nd + 3;
 }
 
@@ -1300,9 +1639,9 @@ bool decode_stream_supported(int T, int D, int F, int K, int E, int has_gate, in
       E + has_gate > 2 * num_sms || num_sms > kMaxCtas)
     return false;
   if (D % 64 || D > 4096 || D < 128 || F % 64 || F > 4096) return false;
-  const int ns = ring_slots_for(T, D, F);
+  const int ns = ring_slots_for(T, D, F, K, num_sms);
   if (ns < 2) return false;
-  const Plan L = make_plan(T, D, F, ns);
+  const Plan L = make_plan(T, D, F, K, num_sms, ns);
   if (L.sd < 1) return false;
   // router rows and order keys live in the ring before the first copy
   if (2u * static_cast<uint32_t>(D) * 4u + static_cast<uint32_t>(T * E) * 4u >
@@ -1314,23 +1653,24 @@ bool decode_stream_supported(int T, int D, int F, int K, int E, int has_gate, in
   if (static_cast<size_t>(T) * R * nd * 4 > static_cast<size_t>(ns) * L.sb) return false;
   if (D % 256 || D / 256 > 16) return false;  // 8-row boxes of D/256 128-byte chunks
   if (D / 64 > 3 * kWarps) return false;       // at most 3 pairs of groups per compute warp
-  return max_stages_bound(T, D, F, K, E, has_shared, num_sms, L.sd) <= kMaxStages;
+  return max_stages_bound(T, D, F, K, E, has_shared, num_sms, L.sd, L.sb) <= kMaxStages;
 }
 
 size_t decode_stream_scratch_bytes(int T, int D, int F, int K) {
   return scratch_layout(T, D, F, K).total;
 }
 
+// [kMaxCtas] per-CTA "acts out" tags, then the tagged act words
 size_t decode_stream_flag_bytes(int T, int F, int K) {
-  return static_cast<size_t>(T * K + 1) * T * (F / 8) * 32;
+  return kMaxCtas * 4 + static_cast<size_t>(T * K + 1) * T * (F / 8) * 32;
 }
 
 cudaError_t launch_decode_stream(const DecodeFusedArgs& a, const DecodeMaps& maps, void* scratch,
                                  void* flags, cudaStream_t s) {
   if (!decode_stream_supported(a.T, a.D, a.F, a.K, a.E, a.has_gate, a.has_shared, a.num_sms))
     return cudaErrorInvalidValue;
-  const int ns = ring_slots_for(a.T, a.D, a.F);
-  const Plan L = make_plan(a.T, a.D, a.F, ns);
+  const int ns = ring_slots_for(a.T, a.D, a.F, a.K, a.num_sms);
+  const Plan L = make_plan(a.T, a.D, a.F, a.K, a.num_sms, ns);
   const ScratchLayout sl = scratch_layout(a.T, a.D, a.F, a.K);
   uint8_t* sc = static_cast<uint8_t*>(scratch);
   StreamParams p{};
@@ -1359,7 +1699,8 @@ cudaError_t launch_decode_stream(const DecodeFusedArgs& a, const DecodeMaps& map
   p.residual = a.residual;
   p.tlogits = static_cast<unsigned long long*>(a.logits);
   p.inv_rms = a.inv_rms;
-  p.hact = reinterpret_cast<unsigned long long*>(flags);
+  p.gdone = static_cast<uint32_t*>(flags);
+  p.hact = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(flags) + kMaxCtas * 4);
   p.partial = reinterpret_cast<float*>(sc + sl.partial);
   p.counters = a.counters;
   p.ids_out = a.ids_out;
