@@ -69,10 +69,12 @@ constexpr int kMaxStages = 96;   // stages of one CTA's share
 constexpr int kMaxRing = 12;     // ring slots
 constexpr int kMaxCtas = 256;
 constexpr int kLogitCopies = 4;
-constexpr int kStamps = 32;
+constexpr int kStamps = 96;
 constexpr int kDownBox = 128;    // rows of the large down box (8 blocks of 16)
 constexpr float kTwo20 = 1048576.0f;
 constexpr int kParts = 3;  // rows owned: each down tile's K split over three work units
+constexpr int kPartsW = 4; // waves: each down tile's K split over four work units
+constexpr int kWavePairs = 4;  // waves: K pairs of one down unit, at most
 
 // Cross-CTA signalling (same scheme as the earlier fused decode kernel):
 // per-CTA launch epochs, the grid counter of each launch parity.
@@ -134,6 +136,11 @@ struct Plan {
   uint32_t act_off;    // [slots][T][F / 8] uint4 act fragments
   uint32_t ast_off;    // [slots][F / 32][T] float accumulator starts
   uint32_t sv_off;     // [slots][T][16 nt] float down results of the CTA's rows
+  // T = 1 router-routed ("waves"): the CTA's rows of every slot's down matrix
+  // in one region (the down results in sv_off)
+  uint32_t down_off;   // [slots][drb] down codes then scales of the CTA's rows
+  uint32_t drb;        // bytes per slot
+  uint32_t nrmax;      // rows of y a CTA owns at most (multiple of 4)
   uint32_t total;      // bytes of the whole plan for `ring` stages
 };
 
@@ -146,7 +153,8 @@ __host__ __device__ inline uint32_t red_words_for(int T) {
   return T == 1 ? 16u : (T == 2 ? 32u : 64u);
 }
 
-__host__ __device__ inline Plan make_plan(int T, int D, int F, int K, int G, int ring) {
+__host__ __device__ inline Plan make_plan(int T, int D, int F, int K, int G, int ring,
+                                          bool waves = false) {
   Plan L;
   uint32_t o = 0;
   L.xf_off = o;
@@ -157,8 +165,19 @@ __host__ __device__ inline Plan make_plan(int T, int D, int F, int K, int G, int
   L.red_off = o;
   L.red_words = red_words_for(T);
   o += static_cast<uint32_t>(ring) * kWarps * L.red_words * 4u;
-  L.act_off = L.ast_off = L.sv_off = o;
-  if (rows_owned(T)) {
+  L.act_off = L.ast_off = L.sv_off = L.down_off = o;
+  L.drb = L.nrmax = 0;
+  if (waves) {
+    const uint32_t slots = static_cast<uint32_t>(K + 1);
+    L.nrmax = 4u * static_cast<uint32_t>((D / 4 + G - 1) / G);
+    o = align_up_u32(o, 16);
+    L.sv_off = o;
+    o += kPartsW * slots * 32u * 4u;
+    L.down_off = o;
+    L.drb = align_up_u32(L.nrmax * static_cast<uint32_t>(F / 2 + F / 16), 16);
+    // (rows past a slot's own, read by a partial last tile, stay inside)
+    o += slots * L.drb + 16u * static_cast<uint32_t>(F / 2 + F / 16);
+  } else if (rows_owned(T)) {
     const uint32_t slots = static_cast<uint32_t>(T * K + 1);
     const uint32_t ntmax = static_cast<uint32_t>((D / 16 + G - 1) / G);
     o = align_up_u32(o, 16);
@@ -365,8 +384,25 @@ TSG_DEV Work make_work(int nslots, int D, int F, int T, uint32_t sb) {
 
 // This CTA's stages: its gate/up blocks, then its down blocks in stages of at
 // most sd blocks of one chunk.  Returns the count (or -1 above kMaxStages).
-TSG_DEV int build_stages(const Work& w, int bid, int G, uint32_t sd, Stage* st) {
+TSG_DEV int build_stages(const Work& w, int bid, int G, uint32_t sd, Stage* st,
+                        bool waves = false) {
   int n = 0;
+  if (waves) {
+    // gate/up blocks dealt round-robin: block i to CTA i mod G, so that the
+    // k-th stages of all CTAs form one wave and each slot's acts complete
+    // early, slot by slot; the down rows are not staged in the ring
+    const uint32_t f8 = w.nc * 8;
+    for (uint32_t b = static_cast<uint32_t>(bid); b < w.ng; b += static_cast<uint32_t>(G)) {
+      if (n >= kMaxStages) return -1;
+      const uint32_t slot = b / f8, rb = b - slot * f8;
+      st[n].kind_slot = static_cast<uint16_t>(slot);
+      st[n].chunk = static_cast<uint16_t>(rb >> 3);
+      st[n].a = static_cast<uint16_t>(rb & 7u);
+      st[n].n = 1;
+      ++n;
+    }
+    return n;
+  }
   const uint32_t ub = static_cast<uint32_t>(bid), ug = static_cast<uint32_t>(G);
   const uint32_t g0 = (w.ng * ub) / ug, g1 = (w.ng * (ub + 1)) / ug;
   const uint32_t f8 = w.nc * 8;
@@ -505,9 +541,81 @@ TSG_DEV void issue_stage(const StreamParams& p, const Plan& L, const Stage& sg, 
 }
 
 // ---------------------------------------------------------------------------
+// waves (one router-routed token): the CTA's rows of y and the slot act
+// loads, kept out of line (each runs a few times per launch; the gate/up
+// loop keeps the instruction cache)
+// ---------------------------------------------------------------------------
+struct WaveRows {
+  const uint8_t* down;  // [slots][drb]: the rows' down codes, then their scales
+  uint32_t drb;
+  float* sv;            // [kPartsW][K + 1][32] the rows' down partials
+  int F, K, nr;         // nr rows (in at most two 16-row tiles)
+};
+
+// One down unit of slot j -- 16-row tile t, pairs [p0, p0 + np) of K -- from
+// the slot's act words: word `lane` of pair p0 + i in v_i.  A pair's 32 words
+// are its eight operand chunks (two groups of 32 acts); the accumulator start
+// of a group is -8 * 2^-20 times the sum of its acts, summed across the
+// lanes that hold them.
+__device__ __noinline__ void wave_unit(const WaveRows& w, int j, int t, int kp, int p0, int np,
+                                       unsigned long long v0, unsigned long long v1,
+                                       unsigned long long v2, unsigned long long v3, int lane) {
+  const int F = w.F, GF = F / 32;
+  const int g = lane >> 2, c = lane & 3, m = lane >> 3, r8 = lane & 7;
+  const uint8_t* dj = w.down + static_cast<uint32_t>(j) * w.drb;
+  const __half* scs =
+      reinterpret_cast<const __half*>(dj + static_cast<uint32_t>(w.nr) * (F / 2)) + 16 * t * GF;
+  const uint32_t rowaddr = smem_u32(dj) + static_cast<uint32_t>(16 * t + r8 + 8 * (m & 1)) * (F / 2) +
+                           static_cast<uint32_t>(m >> 1) * 16u;
+  // words 0, 1 of a chunk hold 16x values
+  const float wscale = c < 2 ? 0.0625f : 1.0f;
+  const unsigned long long wv[kWavePairs] = {v0, v1, v2, v3};
+  float acc0 = 0.0f, acc2 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kWavePairs; ++i) {
+    if (i < np) {
+      const int pr = p0 + i;
+      const uint32_t word = static_cast<uint32_t>(wv[i]);
+      const float2 h = h2_to_f2(word);
+      float gs = (h.x + h.y) * wscale;
+      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 1);
+      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 2);
+      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 4);
+      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 8);
+      const float c00 = -8.0f / kTwo20 * __shfl_sync(0xFFFFFFFFu, gs, 0);
+      const float c10 = -8.0f / kTwo20 * __shfl_sync(0xFFFFFFFFu, gs, 16);
+      uint4 b0, b1;
+      b0.x = __shfl_sync(0xFFFFFFFFu, word, 4 * c);
+      b0.y = __shfl_sync(0xFFFFFFFFu, word, 4 * c + 1);
+      b0.z = __shfl_sync(0xFFFFFFFFu, word, 4 * c + 2);
+      b0.w = __shfl_sync(0xFFFFFFFFu, word, 4 * c + 3);
+      b1.x = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c);
+      b1.y = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c + 1);
+      b1.z = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c + 2);
+      b1.w = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c + 3);
+      if (g != 0) b0 = b1 = make_uint4(0u, 0u, 0u, 0u);  // one token: column 0
+      uint32_t q0, q1, q2, q3;
+      ldsm_x4(rowaddr + static_cast<uint32_t>(pr) * 32u, q0, q1, q2, q3);
+      float d0[4], d1[4];
+      mma_group(d0, q0, q1, b0, c == 0 ? c00 : 0.0f, 0.0f);
+      mma_group(d1, q2, q3, b1, c == 0 ? c10 : 0.0f, 0.0f);
+      const float2 sr = h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + g * GF + 2 * pr));
+      const float2 sh = h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + (g + 8) * GF + 2 * pr));
+      acc0 = fmaf(sr.y, d1[0], fmaf(sr.x, d0[0], acc0));
+      acc2 = fmaf(sh.y, d1[2], fmaf(sh.x, d0[2], acc2));
+    }
+  }
+  if (c == 0) {
+    float* o = w.sv + (static_cast<size_t>(kp) * (w.K + 1) + j) * 32 + 16 * t;
+    o[g] = acc0;
+    o[g + 8] = acc2;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int TT>
+template <int TT, bool WV>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_stream_kernel(const __grid_constant__ StreamParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -516,6 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t bar_rel[kMaxRing];
   __shared__ __align__(8) uint64_t bar_act, bar_act2;  // compute warps, once per launch
   __shared__ __align__(8) uint64_t bar_go;              // warp 0: every CTA's acts are out
+  __shared__ __align__(8) uint64_t bar_down;             // waves: the CTA's down rows have landed
   __shared__ int s_issued[kMaxRing];
   __shared__ Stage s_stage[kMaxStages];
   __shared__ int s_ids[kMaxTok][kMaxK];
@@ -540,10 +649,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int NS = p.ring_slots;
   // one router-selected token: slots follow the ranks, so the weight copies
   // can start as soon as the ranks are known (before softmax and grouping)
-  const bool fast1 = TT == 1 && p.ids_in == nullptr;
+  const bool fast1 = WV || (TT == 1 && p.ids_in == nullptr);
   Signals* sig = reinterpret_cast<Signals*>(p.counters);
   uint32_t* err = p.err;
-  const Plan L = make_plan(T, D, F, K, G, NS);
+  // one router-selected token: the gate/up blocks go out in waves and the
+  // down rows of each slot are done as soon as the slot's acts are out
+  constexpr bool waves = WV;
+  const Plan L = make_plan(T, D, F, K, G, NS, waves);
   uint4* xf = reinterpret_cast<uint4*>(smem + L.xf_off);
   float* cinit = reinterpret_cast<float*>(smem + L.ci_off);
   float* red = reinterpret_cast<float*>(smem + L.red_off);
@@ -565,6 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (tid == 64) s_epoch = __ldcg(&sig->epoch[bid]) + 1u;  // this launch's tag
   if (tid == 96) {
+    mbar_init(&bar_down, 1);
     mbar_init(&bar_act, kWarps);
     mbar_init(&bar_act2, kWarps);
     mbar_init(&bar_go, 1);
@@ -756,7 +869,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (fast1 && warp == kWarps && lane == 0) {
     // the share of one token's layer does not depend on the input: plan it
     // while warp 0 waits for the logits
-    const int n = build_stages(make_work(K + p.has_shared, D, F, T, L.sb), bid, G, L.sd, s_stage);
+    const int n =
+        build_stages(make_work(K + p.has_shared, D, F, T, L.sb), bid, G, L.sd, s_stage, waves);
     s_nst = n;
     if (n < 0) flag_error(err, TSG_DEVERR_BOUNDS);  // the host's shape checks rule this out
   }
@@ -799,6 +913,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         issue_stage(p, L, s_stage[s], s_slot_expert, ring + static_cast<uint32_t>(s) * L.sb,
                     &bar_st[s], lane);
         if (lane == 0) s_issued[s] = 1;
+      }
+      if (waves && warp == kWarps) {
+        // the CTA's rows of every slot's down matrix, codes then scales, one
+        // region for the whole launch (requested after the first gate/up tiles)
+        const int r0 = 4 * ((bid * (D / 4)) / G), nr = 4 * (((bid + 1) * (D / 4)) / G) - r0;
+        const int ns1 = K + p.has_shared;
+        const uint32_t cb = static_cast<uint32_t>(nr) * static_cast<uint32_t>(F / 2);
+        const uint32_t sbytes = static_cast<uint32_t>(nr) * static_cast<uint32_t>(F / 16);
+        if (lane == 0) {
+          if (nr > 0)
+            mbar_arrive_expect_tx(&bar_down, static_cast<uint32_t>(ns1) * (cb + sbytes));
+          else
+            mbar_arrive(&bar_down);
+        }
+        __syncwarp();
+        if (nr > 0)
+          for (int j = lane; j < ns1; j += 32) {
+            const ExpertOffsets* o2;
+            const uint8_t* b2 = slot_blob(p, s_slot_expert[j], &o2);
+            uint8_t* dst = smem + L.down_off + static_cast<uint32_t>(j) * L.drb;
+            bulk_load(dst, b2 + o2->down_w + static_cast<size_t>(r0) * (F / 2), cb, &bar_down);
+            bulk_load(dst + cb, b2 + o2->down_s + static_cast<size_t>(r0) * (F / 16), sbytes,
+                      &bar_down);
+          }
+        __syncwarp();
       }
       stamp(10);
     }
@@ -956,6 +1095,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const int m = lane >> 3, r8 = lane & 7;
   bool failed = false;
+  // ---- waves (T = 1): the CTA's rows of y, slot by slot ----
+  // A compute warp has at most one down unit per slot (unit u of slot j goes
+  // to warp (j U + u) mod 15) and pulls the act words the unit needs into
+  // registers: requested once the slot's last wave is due (after this CTA's
+  // own stage of it), checked after each later gate/up stage, the words not
+  // out yet requested again.  No act passes through shared memory.
+  const int wr0 = 4 * ((bid * (D / 4)) / G);
+  const int wnr = 4 * (((bid + 1) * (D / 4)) / G) - wr0;
+  const int wU = ((wnr + 15) / 16) * kPartsW;
+  float* sv_w = reinterpret_cast<float*>(smem + L.sv_off);
+  WaveRows wrow;
+  wrow.down = smem + L.down_off;
+  wrow.drb = L.drb;
+  wrow.sv = sv_w;
+  wrow.F = F;
+  wrow.K = K;
+  wrow.nr = wnr;
+  bool down_in = false;  // the down region has landed
+  bool wpend = false;    // the act words of slot wj's unit are requested
+  unsigned long long wv0 = 0, wv1 = 0, wv2 = 0, wv3 = 0;
+  int wt = 0, wkp = 0, wp0 = 0, wnp = 0;
+  auto wave_seek = [&](int j) {  // the first slot >= j with a unit of this warp
+    for (; j < nslots; ++j)
+      if (((warp - j * wU) % kWarps + kWarps) % kWarps < wU) break;
+    return j;
+  };
+  int wj = waves ? wave_seek(0) : nslots;
+  auto slot_wave = [&](int j) { return ((j + 1) * F8 - 1) / G; };
+  auto wave_load = [&](bool all) {
+    const unsigned long long* src = p.hact + static_cast<size_t>(wj) * (F / 2) + 32 * wp0 + lane;
+    if (0 < wnp && (all || static_cast<uint32_t>(wv0 >> 32) != tag)) wv0 = ld_relaxed_u64(src);
+    if (1 < wnp && (all || static_cast<uint32_t>(wv1 >> 32) != tag)) wv1 = ld_relaxed_u64(src + 32);
+    if (2 < wnp && (all || static_cast<uint32_t>(wv2 >> 32) != tag)) wv2 = ld_relaxed_u64(src + 64);
+    if (3 < wnp && (all || static_cast<uint32_t>(wv3 >> 32) != tag)) wv3 = ld_relaxed_u64(src + 96);
+  };
+  auto wave_in = [&]() {  // every word of the unit carries this launch's tag
+    const bool ok = (wnp <= 0 || static_cast<uint32_t>(wv0 >> 32) == tag) &&
+                    (wnp <= 1 || static_cast<uint32_t>(wv1 >> 32) == tag) &&
+                    (wnp <= 2 || static_cast<uint32_t>(wv2 >> 32) == tag) &&
+                    (wnp <= 3 || static_cast<uint32_t>(wv3 >> 32) == tag);
+    return __all_sync(0xFFFFFFFFu, ok);
+  };
+  auto wave_start = [&]() {  // the unit of slot wj, and its act words requested
+    const int u = ((warp - wj * wU) % kWarps + kWarps) % kWarps;
+    const int NP2 = F / 64;
+    wt = u / kPartsW;
+    wkp = u - wt * kPartsW;
+    wp0 = (wkp * NP2) / kPartsW;
+    wnp = ((wkp + 1) * NP2) / kPartsW - wp0;
+    wave_load(true);
+    wpend = true;
+  };
+  auto wave_run = [&]() -> bool {  // the unit (once the down rows are in); then the next slot
+    if (!down_in) {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait_inl(&bar_down, 0, err))) return false;
+      down_in = true;
+    }
+    wave_unit(wrow, wj, wt, wkp, wp0, wnp, wv0, wv1, wv2, wv3, lane);
+    wpend = false;
+    wj = wave_seek(wj + 1);
+    return true;
+  };
   const int GF = F / 32;
   uint4* afr = reinterpret_cast<uint4*>(smem + L.act_off);
   float* ast = reinterpret_cast<float*>(smem + L.ast_off);
@@ -1298,6 +1499,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     // release the stage to the reduction warp (which refills its ring slot)
     __syncwarp();
     if (lane == 0) mbar_arrive(&bar_rel[rs]);
+    if (waves)  // between stages: the down units whose acts are in
+      while (wj < nslots) {
+        if (!wpend) {
+          if (s >= slot_wave(wj)) wave_start();  // checked after the next stage
+          break;
+        }
+        if (!wave_in()) {
+          wave_load(false);
+          break;
+        }
+        if (!wave_run()) {
+          failed = true;
+          break;
+        }
+      }
+  }
+  if (waves && !failed) {
+    // the remaining units: one round trip per check
+    const unsigned long long t0 = global_timer_ns();
+    uint32_t spin = 0;
+    while (wj < nslots) {
+      if (!wpend) wave_start();
+      if (!wave_in()) {
+        if ((++spin & 15u) == 0u &&
+            __any_sync(0xFFFFFFFFu, lane == 0 && poll_give_up(t0, err))) {
+          failed = true;
+          break;
+        }
+        wave_load(false);
+        continue;
+      }
+      if (!wave_run()) {
+        failed = true;
+        break;
+      }
+    }
+    stamp(23);  // debug: warp 0's down units done
   }
   } else {
     // the reduction and refill warp: for every stage, once all compute warps
@@ -1307,7 +1545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // flags its acts as out)
     int ngu = 0;
     while (ngu < nst && (s_stage[ngu].kind_slot >> 8) == 0) ++ngu;
-    if (ngu == 0 && lane == 0) {
+    if (ngu == 0 && lane == 0 && !waves) {
       st_relaxed_u32(p.gdone + bid, tag);
       __threadfence();
     }
@@ -1359,7 +1597,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         float hs = 0.0f;
         const uint4 fr = op_chunk(col, &hs);
         const int blk = 8 * sg.chunk + sg.a;
-        if (lane < T) {
+        if (waves) {
+          // four tagged words, no fence: the readers check every tag
+          if (lane == 0) {
+            unsigned long long* o = p.hact + (static_cast<size_t>(slot) * F8 + blk) * 4;
+            const unsigned long long tg = static_cast<unsigned long long>(tag) << 32;
+            st_relaxed_u64(o + 0, tg | fr.x);
+            st_relaxed_u64(o + 1, tg | fr.y);
+            st_relaxed_u64(o + 2, tg | fr.z);
+            st_relaxed_u64(o + 3, tg | fr.w);
+          }
+          __syncwarp();
+          if (s < 8 && lane == 0 && p.stamps) stamp_at(p.stamps, bid * kStamps + 48 + s);  // debug
+
+        } else if (lane < T) {
           // four (tag, half2) words: a reader that sees this launch's tag in
           // a word sees that word's data (no fence, no separate flag)
           unsigned long long* o = p.hact + ((static_cast<size_t>(slot) * T + lane) * F8 + blk) * 4;
@@ -1371,7 +1622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       }
-      if (s == ngu - 1) {
+      if (s == ngu - 1 && !waves) {
         // the block's act words, then the flag: a fence on each side, so that
         // both leave this SM now rather than whenever its store queue drains
         // (once per CTA, on this warp only)
@@ -1397,9 +1648,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (s_failed) {
     // let this CTA's own copies land before it exits; the host clears the
     // signals after reading the error word
-    if (tid == 0)
+    if (tid == 0) {
       for (int i = 0; i < NS; ++i)
         if (s_issued[i] > 0) drain_wait(&bar_st[i], static_cast<uint32_t>(s_issued[i] - 1) & 1u);
+      if (waves && s_nst >= 0) drain_wait(&bar_down, 0);
+    }
+    return;
+  }
+
+  if (waves) {
+    // ---------------- this CTA's rows of y (one token) ----------------
+    // v = the K quarters of a row added in order; y = residual + gate *
+    // shared + sum over ranks (ascending) w * v.  As with owned rows, the
+    // next launch's grid counter is cleared all the same.
+    if (bid == 0 && tid == 0) sig->gcount[(tag & 1u) ^ 1u] = 0u;
+    for (int q = tid; q < wnr; q += kThreads) {
+      auto vs = [&](int j) {
+        float v = 0.0f;
+#pragma unroll
+        for (int kp = 0; kp < kPartsW; ++kp) v += sv_w[(static_cast<size_t>(kp) * (K + 1) + j) * 32 + q];
+        return v * kTwo20;
+      };
+      const int d = wr0 + q;
+      float y = p.residual ? p.residual[d] : 0.0f;
+      if (p.has_shared) {
+        const float v = vs(nslots - 1);
+        y = p.has_gate ? fmaf(s_gate[0], v, y) : y + v;
+      }
+      for (int r = 0; r < K; ++r) y = fmaf(s_w[0][r], vs(r), y);
+      if (p.y_f32)
+        reinterpret_cast<float*>(p.y)[d] = y;
+      else
+        reinterpret_cast<__nv_bfloat16*>(p.y)[d] = __float2bfloat16_rn(y);
+    }
+    stamp(7);
+    if (tid == 0) sig->epoch[bid] = tag;  // read by this CTA's next launch
     return;
   }
 
@@ -1517,10 +1800,11 @@ size_t stream_smem_limit() {
   static size_t limit = 0;
   static std::once_flag once;
   std::call_once(once, [] {
-    const void* kernels[4] = {reinterpret_cast<const void*>(decode_stream_kernel<1>),
-                              reinterpret_cast<const void*>(decode_stream_kernel<2>),
-                              reinterpret_cast<const void*>(decode_stream_kernel<3>),
-                              reinterpret_cast<const void*>(decode_stream_kernel<4>)};
+    const void* kernels[5] = {reinterpret_cast<const void*>(decode_stream_kernel<1, false>),
+                              reinterpret_cast<const void*>(decode_stream_kernel<1, true>),
+                              reinterpret_cast<const void*>(decode_stream_kernel<2, false>),
+                              reinterpret_cast<const void*>(decode_stream_kernel<3, false>),
+                              reinterpret_cast<const void*>(decode_stream_kernel<4, false>)};
     size_t lim = ~static_cast<size_t>(0);
     for (const void* k : kernels) {
       if (allow_max_smem_ptr(k) != cudaSuccess) return;
@@ -1534,11 +1818,26 @@ size_t stream_smem_limit() {
 }
 
 // Ring stages for this shape within the shared memory limit (0: does not fit).
-int ring_slots_for(int T, int D, int F, int K, int G) {
+int ring_slots_for(int T, int D, int F, int K, int G, bool waves = false) {
   const size_t lim = stream_smem_limit();
   for (int ns = kMaxRing; ns >= 2; --ns)
-    if (make_plan(T, D, F, K, G, ns).total <= lim) return ns;
+    if (make_plan(T, D, F, K, G, ns, waves).total <= lim) return ns;
   return 0;
+}
+
+// Whether one router-routed token can run in waves: a down unit's pairs at
+// most kWavePairs (one act word per lane each), a CTA's rows of y in two
+// 16-row tiles, the whole plan in shared memory with room for the router
+// rows and order keys.
+bool waves_ok(int D, int F, int K, int E, int G) {
+  if (F / 64 > kPartsW * kWavePairs || F / 64 < kPartsW) return false;
+  if (4 * ((D / 4 + G - 1) / G) > 32) return false;
+  if ((static_cast<long long>(K + 1) * (F / 8) + G - 1) / G > kMaxStages) return false;
+  const int ns = ring_slots_for(1, D, F, K, G, true);
+  if (ns < 2) return false;
+  const Plan L = make_plan(1, D, F, K, G, ns, true);
+  return 2u * static_cast<uint32_t>(D) * 4u + static_cast<uint32_t>(E) * 4u <=
+         static_cast<uint32_t>(ns) * L.sb;
 }
 
 // An upper bound of the stages of one CTA's share (largest slot count).
@@ -1669,8 +1968,9 @@ cudaError_t launch_decode_stream(const DecodeFusedArgs& a, const DecodeMaps& map
                                  void* flags, cudaStream_t s) {
   if (!decode_stream_supported(a.T, a.D, a.F, a.K, a.E, a.has_gate, a.has_shared, a.num_sms))
     return cudaErrorInvalidValue;
-  const int ns = ring_slots_for(a.T, a.D, a.F, a.K, a.num_sms);
-  const Plan L = make_plan(a.T, a.D, a.F, a.K, a.num_sms, ns);
+  const bool waves = a.T == 1 && a.ids_in == nullptr && waves_ok(a.D, a.F, a.K, a.E, a.num_sms);
+  const int ns = ring_slots_for(a.T, a.D, a.F, a.K, a.num_sms, waves);
+  const Plan L = make_plan(a.T, a.D, a.F, a.K, a.num_sms, ns, waves);
   const ScratchLayout sl = scratch_layout(a.T, a.D, a.F, a.K);
   uint8_t* sc = static_cast<uint8_t*>(scratch);
   StreamParams p{};
@@ -1724,10 +2024,12 @@ cudaError_t launch_decode_stream(const DecodeFusedArgs& a, const DecodeMaps& map
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
   switch (a.T) {
-    case 1: return cudaLaunchKernelEx(&cfg, decode_stream_kernel<1>, p);
-    case 2: return cudaLaunchKernelEx(&cfg, decode_stream_kernel<2>, p);
-    case 3: return cudaLaunchKernelEx(&cfg, decode_stream_kernel<3>, p);
-    default: return cudaLaunchKernelEx(&cfg, decode_stream_kernel<4>, p);
+    case 1:
+      return waves ? cudaLaunchKernelEx(&cfg, decode_stream_kernel<1, true>, p)
+                   : cudaLaunchKernelEx(&cfg, decode_stream_kernel<1, false>, p);
+    case 2: return cudaLaunchKernelEx(&cfg, decode_stream_kernel<2, false>, p);
+    case 3: return cudaLaunchKernelEx(&cfg, decode_stream_kernel<3, false>, p);
+    default: return cudaLaunchKernelEx(&cfg, decode_stream_kernel<4, false>, p);
   }
 }
 
