@@ -251,13 +251,11 @@ TSG_DEV bool mbar_wait_inl(uint64_t* bar, uint32_t parity, uint32_t* err) {
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 63u) == 0u) {
-      if (error_raised(err)) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        flag_error(err, TSG_DEVERR_TIMEOUT);
-        return false;
-      }
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      flag_error(err, TSG_DEVERR_TIMEOUT);
+      return false;
     }
+    if ((++spins & 15u) == 0u && error_raised(err)) return false;
   }
   return true;
 }

@@ -323,13 +323,11 @@ TSG_DEV bool mbar_wait_inl(uint64_t* bar, uint32_t parity, uint32_t* err) {
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 63u) == 0u) {
-      if (error_raised(err)) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        flag_error(err, TSG_DEVERR_TIMEOUT);
-        return false;
-      }
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      flag_error(err, TSG_DEVERR_TIMEOUT);
+      return false;
     }
+    if ((++spins & 15u) == 0u && error_raised(err)) return false;
   }
   return true;
 }
@@ -636,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_pos_slot[kMaxPairs + kMaxTok], s_pos_col[kMaxPairs + kMaxTok];
   __shared__ float s_inv[kMaxTok], s_gate[kMaxTok];
   __shared__ float s_red[2 * kMaxTok][kAllWarps];
-  __shared__ int s_nslots, s_nst, s_failed;
+  __shared__ int s_nslots, s_nst, s_failed, s_down_issued;
   __shared__ uint32_t s_epoch;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -693,6 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   &bar_rw);
     }
     s_failed = 0;
+    s_down_issued = 0;
     s_nslots = 0;
     if (fast1) {
       // one token routed by this kernel: K distinct experts in rank order
@@ -938,6 +937,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       &bar_down);
           }
         __syncwarp();
+        if (lane == 0) s_down_issued = 1;
       }
       stamp(10);
     }
@@ -1104,6 +1104,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int wr0 = 4 * ((bid * (D / 4)) / G);
   const int wnr = 4 * (((bid + 1) * (D / 4)) / G) - wr0;
   const int wU = ((wnr + 15) / 16) * kPartsW;
+  // this thread's row of the residual, read long before the combine
+  const float wres = waves && p.residual && tid < wnr ? p.residual[wr0 + tid] : 0.0f;
   float* sv_w = reinterpret_cast<float*>(smem + L.sv_off);
   WaveRows wrow;
   wrow.down = smem + L.down_off;
@@ -1527,6 +1529,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           failed = true;
           break;
         }
+        // (every CTA's waiting warps poll the same few lines: space the polls)
+        __nanosleep(256);
         wave_load(false);
         continue;
       }
@@ -1651,7 +1655,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
       for (int i = 0; i < NS; ++i)
         if (s_issued[i] > 0) drain_wait(&bar_st[i], static_cast<uint32_t>(s_issued[i] - 1) & 1u);
-      if (waves && s_nst >= 0) drain_wait(&bar_down, 0);
+      if (s_down_issued) drain_wait(&bar_down, 0);
     }
     return;
   }
@@ -1670,7 +1674,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return v * kTwo20;
       };
       const int d = wr0 + q;
-      float y = p.residual ? p.residual[d] : 0.0f;
+      float y = q == tid ? wres : (p.residual ? p.residual[d] : 0.0f);
       if (p.has_shared) {
         const float v = vs(nslots - 1);
         y = p.has_gate ? fmaf(s_gate[0], v, y) : y + v;

@@ -98,11 +98,29 @@ TSG_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One try of a phase: the thread may be suspended until the phase completes
+// or kTryWaitHintNs pass.  The bound is explicit: without one the suspend
+// limit is the system's choice, and a wait loop that checks its clock between
+// tries could then overrun its own limit by far.
+constexpr uint32_t kTryWaitHintNs = 10000u;
 TSG_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitHintNs)
+      : "memory");
+  return ok != 0u;
+}
+
+// Non-blocking test of a phase (for a look ahead that must not stall).
+TSG_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -118,13 +136,11 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 63u) == 0u) {
-      if (error_raised(err)) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        flag_error(err, TSG_DEVERR_TIMEOUT);
-        return false;
-      }
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      flag_error(err, TSG_DEVERR_TIMEOUT);
+      return false;
     }
+    if ((++spins & 15u) == 0u && error_raised(err)) return false;
   }
   return true;
 }

@@ -339,8 +339,8 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
           Ring na = ra, nb = rb;
           na.next(kAStages);
           nb.next(SB);
-          ready = j + 1 < stages_per_item && mbar_try_wait(&sm.full_a[na.s], na.ph) &&
-                  mbar_try_wait(&sm.full_b[nb.s], nb.ph);
+          ready = j + 1 < stages_per_item && mbar_test_wait(&sm.full_a[na.s], na.ph) &&
+                  mbar_test_wait(&sm.full_b[nb.s], nb.ph);
           umma_commit(&sm.empty_a[ra.s]);
           umma_commit(&sm.empty_b[rb.s]);
         }
