@@ -274,7 +274,7 @@ def run_ours(args):
     ms_max = float(ms_t.item())
     value = world * T * LAYERS / (ms_max / 1e3)
 
-    # dominant kernel: at T=1 the whole layer is one kernel (decode_fused_kernel),
+    # dominant kernel: at T=1 the whole layer is one kernel (decode_stream_kernel),
     # and the timed graph holds nothing but its 30 launches, so the average
     # launch duration is the CUDA-event time of the timed replays / 30 (an
     # upper bound: it includes the gaps between launches).  The profiled
@@ -292,7 +292,7 @@ def run_ours(args):
     tfile = ROOT / "profiles" / "ncu_traffic.json"
     if tfile.exists():
         tj = json.loads(tfile.read_text())
-        traffic = tj.get("decode_fused_t1_bytes_per_launch")
+        traffic = tj.get("decode_stream_t1_bytes_per_launch")
 
     # end to end through the public API: pinned host input -> stack -> host
     x_host = torch.empty((T, D), dtype=torch.bfloat16, pin_memory=True)
@@ -355,7 +355,7 @@ def run_ours(args):
             "graph": "CUDA graph of the 30-layer step",
         },
         "roofline": {
-            "kernel": "decode_fused_kernel (T=1, whole layer)",
+            "kernel": "decode_stream_kernel<1, waves> (T=1, whole layer)",
             "bound": "hbm",
             "achieved": achieved,
             "peak": pk["hbm_gbs"],
