@@ -162,6 +162,19 @@ TSG_API tsg_status tsg_moe_block_forward(tsg_ctx ctx, tsg_moe_layer layer, const
                                  uint32_t hidden_stride, uint32_t T, const float *residual_f32,
                                  void *y, uint32_t y_stride, tsg_dtype y_dtype);
 
+/* A speculative-verify block of T rows, each row's y bit for bit what
+ * tsg_moe_block_forward gives that row alone in the decode regime (T = 1):
+ * "a verify block is decode generalized to k rows".  Replaces
+ * PrefillGroupedRoutedMoE.encodeStreamedRows / usesExpertRowsPath
+ * (PrefillGroupedRoutedMoE.swift:768-800), whose contract is pinned by
+ * PrefillRoutedMoERowsVsDecodeTests.swift:23-166.  Runs the streaming decode
+ * kernel on the rows two at a time; TSG_ERR_UNSUPPORTED_SHAPE when that
+ * kernel does not take the layer (or option fused_decode is not 1).
+ * Arguments as tsg_moe_block_forward. */
+TSG_API tsg_status tsg_moe_verify_rows_forward(tsg_ctx ctx, tsg_moe_layer layer, const void *hidden_bf16,
+                                       uint32_t hidden_stride, uint32_t T, const float *residual_f32,
+                                       void *y, uint32_t y_stride, tsg_dtype y_dtype);
+
 /* Router + top-K.  Replaces MoE.encodeRouterGemma4BF16 (MoE.swift:259-302),
  * encodeRouterGemma4BF16Rows (:413-466), PrefillRouter.encodeGemma4BF16Block
  * and encodeGemma4BF16GEMM (PrefillRouter.swift:127-236).  Outputs [T][K]:

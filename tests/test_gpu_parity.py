@@ -428,3 +428,41 @@ def test_bf16_output_and_residual(ctx):
     ctx.sync()
     y_ref, _, _ = ol.block(x, ids.cpu().numpy().astype(np.uint32), w.cpu().numpy())
     assert rel_l2(y.float().cpu().numpy(), y_ref + resid) <= REL_L2
+
+
+@pytest.mark.parametrize("name,T", [("gemma", 1), ("gemma", 2), ("gemma", 5), ("qwen", 3),
+                                    ("qwen", 8), ("tiny", 4)])
+def test_verify_rows_bit_equal_to_decode(ctx, name, T):
+    """A speculative-verify block gives every row decode's bits: the rows
+    path against T single-token forwards, compared bit for bit (as
+    PrefillRoutedMoERowsVsDecodeTests.swift:23-166 compares the reference's
+    rows path with its decode kernels), with and without a residual; and the
+    block against the oracle."""
+    host, dev, ol = layer_pair(ctx, name, 11, None)
+    x = host_tokens(T, host.d, 300 + T)
+    xd = to_dev(x)
+    g = torch.Generator(device="cpu").manual_seed(5 + T)
+    res = torch.randn((T, host.d), generator=g).cuda()
+    with regime(ctx, 4, True):
+        for r in (None, res):
+            y = dev.verify_rows(xd, residual=r, out_dtype=torch.float32)
+            ctx.sync()
+            rows = [dev.forward(xd[i:i + 1], residual=None if r is None else r[i:i + 1],
+                                out_dtype=torch.float32) for i in range(T)]
+            ctx.sync()
+            ref = torch.cat(rows)
+            diff = (y != ref).sum().item()
+            assert diff == 0, f"{diff} of {y.numel()} outputs differ from decode"
+            if r is None:
+                y0 = y
+        ybf = dev.verify_rows(xd)
+        ctx.sync()
+        rows = [dev.forward(xd[i:i + 1]) for i in range(T)]
+        ctx.sync()
+        assert torch.equal(ybf.view(torch.int16), torch.cat(rows).view(torch.int16))
+    ids, w, _ = gpu_route(ctx, dev, xd)
+    ref_ids, _, gap, _ = ol.router(x)
+    ok = gap >= TIE_GAP
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32)[ok], ref_ids[ok])
+    y_ref, _, _ = ol.block(x, ids.cpu().numpy().astype(np.uint32), w.cpu().numpy())
+    assert rel_l2(y0.cpu().numpy(), y_ref) <= REL_L2

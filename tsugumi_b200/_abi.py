@@ -83,6 +83,7 @@ SIGNATURES = [
     ("tsg_moe_layer_create", _S, [_P, C.POINTER(LayerDesc), C.POINTER(_P)]),
     ("tsg_moe_layer_destroy", _S, [_P]),
     ("tsg_moe_block_forward", _S, [_P, _P, _P, _U, _U, _P, _P, _U, C.c_int]),
+    ("tsg_moe_verify_rows_forward", _S, [_P, _P, _P, _U, _U, _P, _P, _U, C.c_int]),
     ("tsg_router_topk", _S, [_P, _P, _P, _U, _U, _P, _P, _P]),
     ("tsg_router_logits", _S, [_P, _P, _P, _U, _U, _P]),
     ("tsg_make_token_expert_pairs", _S, [_P, _P, _P, _U, _U, _P]),

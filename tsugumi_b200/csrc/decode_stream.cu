@@ -72,8 +72,10 @@ constexpr int kLogitCopies = 4;
 constexpr int kStamps = 96;
 constexpr int kDownBox = 128;    // rows of the large down box (8 blocks of 16)
 constexpr float kTwo20 = 1048576.0f;
-constexpr int kParts = 3;  // rows owned: each down tile's K split over three work units
-constexpr int kPartsW = 4; // waves: each down tile's K split over four work units
+// A down tile's K is split over four work units, their partials added in
+// unit order; the same split in every regime (T = 1 waves, rows owned), so
+// that one token's down rows come out of the same arithmetic either way.
+constexpr int kParts = 4;
 constexpr int kWavePairs = 4;  // waves: K pairs of one down unit, at most
 
 // Cross-CTA signalling (same scheme as the earlier fused decode kernel):
@@ -172,7 +174,7 @@ __host__ __device__ inline Plan make_plan(int T, int D, int F, int K, int G, int
     L.nrmax = 4u * static_cast<uint32_t>((D / 4 + G - 1) / G);
     o = align_up_u32(o, 16);
     L.sv_off = o;
-    o += kPartsW * slots * 32u * 4u;
+    o += kParts * slots * 32u * 4u;
     L.down_off = o;
     L.drb = align_up_u32(L.nrmax * static_cast<uint32_t>(F / 2 + F / 16), 16);
     // (rows past a slot's own, read by a partial last tile, stay inside)
@@ -538,6 +540,23 @@ TSG_DEV void issue_stage(const StreamParams& p, const Plan& L, const Stage& sg, 
   __syncwarp();
 }
 
+// The sum of one group's 32 acts from its four operand chunks (words 0, 1 of
+// a chunk hold 16x values), as a balanced tree over the 16 words: the order
+// a 16-lane butterfly of shuffles gives, so that the waves regime (which sums
+// across lanes) and the rows-owned regime (which sums in one thread) agree
+// bit for bit.
+TSG_DEV float group_act_sum(const uint4* fr) {
+  float a[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 u = fr[i];
+    const float2 h0 = h2_to_f2(u.x), h1 = h2_to_f2(u.y);
+    const float2 h2 = h2_to_f2(u.z), h3 = h2_to_f2(u.w);
+    a[i] = ((h0.x + h0.y) * 0.0625f + (h1.x + h1.y) * 0.0625f) + ((h2.x + h2.y) + (h3.x + h3.y));
+  }
+  return (a[0] + a[1]) + (a[2] + a[3]);
+}
+
 // ---------------------------------------------------------------------------
 // waves (one router-routed token): the CTA's rows of y and the slot act
 // loads, kept out of line (each runs a few times per launch; the gate/up
@@ -546,7 +565,7 @@ TSG_DEV void issue_stage(const StreamParams& p, const Plan& L, const Stage& sg, 
 struct WaveRows {
   const uint8_t* down;  // [slots][drb]: the rows' down codes, then their scales
   uint32_t drb;
-  float* sv;            // [kPartsW][K + 1][32] the rows' down partials
+  float* sv;            // [kParts][K + 1][32] the rows' down partials
   int F, K, nr;         // nr rows (in at most two 16-row tiles)
 };
 
@@ -1103,7 +1122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // out yet requested again.  No act passes through shared memory.
   const int wr0 = 4 * ((bid * (D / 4)) / G);
   const int wnr = 4 * (((bid + 1) * (D / 4)) / G) - wr0;
-  const int wU = ((wnr + 15) / 16) * kPartsW;
+  const int wU = ((wnr + 15) / 16) * kParts;
   // this thread's row of the residual, read long before the combine
   const float wres = waves && p.residual && tid < wnr ? p.residual[wr0 + tid] : 0.0f;
   float* sv_w = reinterpret_cast<float*>(smem + L.sv_off);
@@ -1142,10 +1161,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto wave_start = [&]() {  // the unit of slot wj, and its act words requested
     const int u = ((warp - wj * wU) % kWarps + kWarps) % kWarps;
     const int NP2 = F / 64;
-    wt = u / kPartsW;
-    wkp = u - wt * kPartsW;
-    wp0 = (wkp * NP2) / kPartsW;
-    wnp = ((wkp + 1) * NP2) / kPartsW - wp0;
+    wt = u / kParts;
+    wkp = u - wt * kParts;
+    wp0 = (wkp * NP2) / kParts;
+    wnp = ((wkp + 1) * NP2) / kParts - wp0;
     wave_load(true);
     wpend = true;
   };
@@ -1295,16 +1314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q = warp * 32 + lane; q < na; q += kWarps * 32) {
           const int st_ = q / GF, grp = q - st_ * GF;  // st_ = slot * T + t
           const uint4* fr = afr + static_cast<size_t>(st_) * F8 + 4 * grp;
-          float sm = 0.0f;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 u = fr[i];
-            const float2 h0 = h2_to_f2(u.x), h1 = h2_to_f2(u.y);
-            const float2 h2 = h2_to_f2(u.z), h3 = h2_to_f2(u.w);
-            sm += ((h0.x + h0.y) + (h1.x + h1.y)) * 0.0625f + ((h2.x + h2.y) + (h3.x + h3.y));
-          }
           const int sl = st_ / T, t = st_ - sl * T;
-          ast[(static_cast<size_t>(sl) * GF + grp) * T + t] = -8.0f / kTwo20 * sm;
+          ast[(static_cast<size_t>(sl) * GF + grp) * T + t] = -8.0f / kTwo20 * group_act_sum(fr);
         }
       }
       __syncwarp();
@@ -1670,7 +1681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto vs = [&](int j) {
         float v = 0.0f;
 #pragma unroll
-        for (int kp = 0; kp < kPartsW; ++kp) v += sv_w[(static_cast<size_t>(kp) * (K + 1) + j) * 32 + q];
+        for (int kp = 0; kp < kParts; ++kp) v += sv_w[(static_cast<size_t>(kp) * (K + 1) + j) * 32 + q];
         return v * kTwo20;
       };
       const int d = wr0 + q;
@@ -1834,7 +1845,7 @@ int ring_slots_for(int T, int D, int F, int K, int G, bool waves = false) {
 // 16-row tiles, the whole plan in shared memory with room for the router
 // rows and order keys.
 bool waves_ok(int D, int F, int K, int E, int G) {
-  if (F / 64 > kPartsW * kWavePairs || F / 64 < kPartsW) return false;
+  if (F / 64 > kParts * kWavePairs || F / 64 < kParts) return false;
   if (4 * ((D / 4 + G - 1) / G) > 32) return false;
   if ((static_cast<long long>(K + 1) * (F / 8) + G - 1) / G > kMaxStages) return false;
   const int ns = ring_slots_for(1, D, F, K, G, true);

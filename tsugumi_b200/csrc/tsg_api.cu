@@ -1206,6 +1206,42 @@ tsg_status tsg_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidde
   return r;
 }
 
+// A speculative-verify block, row by row as decode computes it: the rows go
+// through the streaming decode kernel two at a time (one for an odd last
+// row).  That kernel's down split, reduction orders and accumulator starts
+// are the same for one and two tokens, and an MMA column does not see its
+// neighbours, so each row's y has the bits tsg_moe_block_forward gives that
+// row alone.
+tsg_status tsg_moe_verify_rows_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
+                                       uint32_t hidden_stride, uint32_t T, const float* residual,
+                                       void* y, uint32_t y_stride, tsg_dtype y_dtype) {
+  tsg_status st = check_common(ctx, L, hidden, hidden_stride, T, y, y_stride, y_dtype);
+  if (st != TSG_OK || T == 0) return st;
+  st = take_pending_error(ctx);
+  if (st != TSG_OK) return st;
+  if (!stream_ok(ctx, L, 1) || (T > 1 && !stream_ok(ctx, L, 2)))
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE,
+                "verify rows need the streaming decode kernel (option fused_decode = 1) for this shape");
+  st = ensure_workspace(ctx, layer_caps(L, T < 2 ? 2 : T));
+  if (st != TSG_OK) return st;
+  ctx->last_T = T;
+  ctx->last_K = L->desc.top_k;
+  const size_t K = L->desc.top_k, D = L->desc.d;
+  const size_t ysz = y_dtype == TSG_DTYPE_F32 ? 4 : 2;
+  prof_mark(ctx, 0);
+  for (uint32_t i = 0; i < T; i += 2) {
+    const uint32_t n = T - i < 2 ? T - i : 2;
+    st = run_decode_fused(ctx, L, static_cast<const uint8_t*>(hidden) + static_cast<size_t>(i) * hidden_stride * 2,
+                          hidden_stride, n, nullptr, nullptr, residual ? residual + i * D : nullptr,
+                          static_cast<uint8_t*>(y) + static_cast<size_t>(i) * y_stride * ysz, y_stride,
+                          y_dtype, ctx->rb.ids + i * K, ctx->rb.weights + i * K,
+                          ctx->rb.weights_f16 + i * K);
+    if (st != TSG_OK) return st;
+  }
+  if (ctx->profiling && ctx->prof_calls < ctx->prof_max) ++ctx->prof_calls;
+  return TSG_OK;
+}
+
 tsg_status tsg_ctx_profile_begin(tsg_ctx ctx, uint32_t max_calls) {
   if (!ctx || max_calls == 0) return fail(ctx, TSG_ERR_INVALID_ARG, "max_calls must be positive");
   cudaSetDevice(ctx->device);

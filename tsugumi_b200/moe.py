@@ -137,6 +137,20 @@ class MoELayer:
               self.ctx.h)
         return y
 
+    def verify_rows(self, hidden, y=None, residual=None, out_dtype=None):
+        """tsg_moe_verify_rows_forward: a speculative-verify block, each row
+        bit-equal to forward() on that row alone (PrefillGroupedRoutedMoE
+        .encodeStreamedRows, PrefillGroupedRoutedMoE.swift:768-800)."""
+        T = hidden.shape[0]
+        if y is None:
+            y = torch.empty((T, self.d), dtype=out_dtype or torch.bfloat16, device=hidden.device)
+        dt = _abi.DTYPE_F32 if y.dtype == torch.float32 else _abi.DTYPE_BF16
+        check(self.ctx.lib.tsg_moe_verify_rows_forward(self.ctx.h, self.h, _ptr(hidden),
+                                                       hidden.stride(0), T, _ptr(residual),
+                                                       _ptr(y), y.stride(0), dt),
+              self.ctx.h)
+        return y
+
     def close(self) -> None:
         if self.h:
             self.ctx.lib.tsg_moe_layer_destroy(self.h)
