@@ -112,9 +112,14 @@ typedef struct tsg_moe_layer_desc {
     uint32_t router_norm;          /* 1: no-scale RMSNorm of the block input */
     float norm_eps;
     const void *shared_expert;     /* optional shared expert blob, NULL if none */
-    uint32_t shared_f;             /* must equal f when present */
+    uint32_t shared_f;             /* its intermediate width (multiple of 64): equal to f,
+                                      a shared expert (a slot of the routed kernels);
+                                      else a dense branch (Gemma's dense MLP,
+                                      SharedExpertInt4.swift:30-94), run beside the
+                                      routed experts and added: y = residual + dense(x)
+                                      + sum_r w_r expert_r(x) */
     tsg_expert_offsets shared_offsets;
-    const float *shared_gate;      /* [D] sigmoid gate vector, or NULL */
+    const float *shared_gate;      /* [D] sigmoid gate vector, or NULL (shared_f == f only) */
 } tsg_moe_layer_desc;
 
 /* ---- context (MetalContext analogue, Infrastructure/Metal/MetalContext.swift) ---- */

@@ -239,6 +239,13 @@ BLOCK_CASES = [
     ("gemma", 64, 1.1, 4, True, None),
     ("qwen", 33, None, 4, True, None),
     ("qwen", 64, None, 4, True, None),
+    # Gemma with its dense MLP branch (F = 2112 beside the experts' 704):
+    # decode kernels, batched GEMVs and the tcgen05 contraction for the branch
+    ("gemma_dense", 1, None, 4, True, None),
+    ("gemma_dense", 3, None, 4, True, None),
+    ("gemma_dense", 12, None, 4, True, None),
+    ("gemma_dense", 300, None, 4, True, 48),
+    ("gemma_dense", 8, None, 64, False, None),
 ]
 
 
@@ -386,9 +393,12 @@ def test_experts_with_caller_routing(ctx, which, T, hot):
     assert rel_l2(y.cpu().numpy(), y_ref + resid) <= REL_L2
 
 
-@pytest.mark.parametrize("T", [1, 100])
-def test_shared_expert_alone(ctx, T):
-    host, dev, ol = layer_pair(ctx, "qwen", 11, None)
+@pytest.mark.parametrize("name,T", [("qwen", 1), ("qwen", 100), ("gemma_dense", 1),
+                                    ("gemma_dense", 100)])
+def test_shared_expert_alone(ctx, name, T):
+    """SharedExpertRuntime alone: Qwen's shared expert, and Gemma's dense
+    branch (SharedExpertInt4.swift:30-94) whose F differs from the experts'."""
+    host, dev, ol = layer_pair(ctx, name, 11, None)
     x = host_tokens(T, host.d, 21)
     y = torch.empty((T, host.d), dtype=torch.float32, device="cuda")
     tb.SharedExpertRuntime(ctx, dev).encode(to_dev(x), y)
@@ -431,7 +441,7 @@ def test_bf16_output_and_residual(ctx):
 
 
 @pytest.mark.parametrize("name,T", [("gemma", 1), ("gemma", 2), ("gemma", 5), ("qwen", 3),
-                                    ("qwen", 8), ("tiny", 4)])
+                                    ("qwen", 8), ("tiny", 4), ("gemma_dense", 3)])
 def test_verify_rows_bit_equal_to_decode(ctx, name, T):
     """A speculative-verify block gives every row decode's bits: the rows
     path against T single-token forwards, compared bit for bit (as

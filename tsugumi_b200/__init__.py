@@ -34,8 +34,9 @@ def upload_host_layer(host, device: int = 0) -> dict:
     }
     if host.shared is not None:
         t.update(shared=torch.from_numpy(host.shared).to(dev), shared_f=host.shared_f,
-                 shared_offsets=host.shared_offsets,
-                 shared_gate=torch.from_numpy(host.shared_gate).to(dev))
+                 shared_offsets=host.shared_offsets)
+        if host.shared_gate is not None:
+            t["shared_gate"] = torch.from_numpy(host.shared_gate).to(dev)
     if host.logit_bias is not None:
         t["logit_bias"] = torch.from_numpy(host.logit_bias).to(dev)
     return t

@@ -30,8 +30,9 @@ namespace {
 // Workspace capacity in elements of each dimension.
 struct Caps {
   uint32_t T = 0, D = 0, F = 0, E = 0, K = 0;
+  uint32_t dense = 0;  // 1: a layer with a dense branch (its routed result is staged in f32)
   bool covers(const Caps& o) const {
-    return T >= o.T && D >= o.D && F >= o.F && E >= o.E && K >= o.K;
+    return T >= o.T && D >= o.D && F >= o.F && E >= o.E && K >= o.K && dense >= o.dense;
   }
   Caps max_with(const Caps& o) const {
     Caps c;
@@ -40,6 +41,7 @@ struct Caps {
     c.F = std::max(F, o.F);
     c.E = std::max(E, o.E);
     c.K = std::max(K, o.K);
+    c.dense = std::max(dense, o.dense);
     return c;
   }
 };
@@ -63,6 +65,7 @@ struct tsg_ctx_s {
   __half* act_buf = nullptr;
   __half* xp = nullptr;
   __half* partials = nullptr;
+  float* dense_y = nullptr;  // [T][D] f32: a dense-branch layer's routed result
   // fused decode scratch
   void* f_logits = nullptr;  // fused decode: tagged logits
   size_t f_logits_bytes = 0;
@@ -110,6 +113,10 @@ struct tsg_moe_layer_s {
   int has_shared = 0;
   DecodeMaps dmaps{};       // down-slice tensor maps of the streaming decode kernel
   bool dmaps_ok = false;
+  // the dense branch (a shared int4 MLP whose F differs from the experts',
+  // Gemma's dense MLP): a one-expert view of it, run beside the routed
+  // experts and added to their result; owned
+  tsg_moe_layer_s* dense = nullptr;
 };
 
 EncodeTiledFn tsg::encode_tiled_fn() {
@@ -207,6 +214,7 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
   __half* act = static_cast<__half*>(take(rows * F * 2));
   __half* xp = static_cast<__half*>(take(rows * D * 2));
   __half* part = static_cast<__half*>(take(rows * D * 2));
+  float* dense_y = static_cast<float*>(take(c.dense ? T * D * 4 : 0));
   // fused decode (T <= 4)
   const size_t Tf = std::min<size_t>(T, 4);
   const size_t rows_f = Tf * K + Tf;
@@ -235,6 +243,7 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
     ctx->act_buf = act;
     ctx->xp = xp;
     ctx->partials = part;
+    ctx->dense_y = c.dense ? dense_y : nullptr;
   }
   return align_up(off, 256);
 }
@@ -267,6 +276,10 @@ Caps layer_caps(const tsg_moe_layer_s* L, uint32_t T) {
   c.F = L->desc.f;
   c.E = L->desc.num_experts;
   c.K = std::max<uint32_t>(L->desc.top_k, 1);
+  if (L->dense) {
+    c.F = std::max(c.F, L->dense->desc.f);
+    c.dense = 1;
+  }
   return c;
 }
 
@@ -514,6 +527,34 @@ tsg_status run_prefill_experts(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, u
   TSG_CUDA_TRY(ctx, launch_combine(cp, ctx->stream), "combine");
   prof_mark(ctx, 4);
   return TSG_OK;
+}
+
+__global__ void dense_route_kernel(uint32_t* ids, float* w, uint16_t* w16, int T) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x) {
+    ids[i] = 0u;
+    w[i] = 1.0f;
+    w16[i] = 0x3C00u;  // fp16 1.0
+  }
+}
+
+// A layer's dense branch (SharedExpertInt4.encode, SharedExpertInt4.swift:
+// 30-94: gate and up GEMVs, act(g)·u, the down GEMV, on every token):
+// y = residual + dense(x), through the one-expert view of the layer that
+// every token takes with weight 1 -- the batched int4 GEMVs for up to
+// gemv_max_tokens tokens (its wide F does not fit the decode kernels'
+// shared-memory plan), else the tcgen05 contraction.  The input is the
+// routed experts' (the no-scale RMSNorm when the layer normalises).
+tsg_status run_dense_branch(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint32_t x_stride,
+                            uint32_t T, const float* residual, void* y, uint32_t y_stride,
+                            tsg_dtype y_dtype) {
+  tsg_moe_layer_s* Dn = L->dense;
+  const int blocks = static_cast<int>(std::min<uint32_t>((T + 255) / 256, 148u));
+  dense_route_kernel<<<blocks, 256, 0, ctx->stream>>>(ctx->rb.ids, ctx->rb.weights,
+                                                      ctx->rb.weights_f16, static_cast<int>(T));
+  TSG_CUDA_TRY(ctx, cudaGetLastError(), "dense branch routing");
+  const RouterParams p = router_params(Dn, x, x_stride, T);
+  TSG_CUDA_TRY(ctx, launch_rowprep(p, ctx->rb, 0, ctx->stream), "row prep (dense branch)");
+  return run_prefill_experts(ctx, Dn, x, x_stride, T, residual, y, y_stride, y_dtype, true);
 }
 
 tsg_status check_common(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32_t x_stride,
@@ -835,8 +876,13 @@ tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc* d, tsg_mo
                               o.down_w_off | o.down_s_off;
   if (align_bits & 15u)
     return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "expert blobs and sub-tensors must be 16-byte aligned");
+  const bool dense = d->shared_expert && d->shared_f != d->f;
   if (d->shared_expert) {
-    if (d->shared_f != d->f) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "shared F must equal F");
+    if (d->shared_f == 0 || d->shared_f % 64)
+      return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "shared F must be a multiple of 64");
+    if (dense && d->shared_gate)
+      return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE,
+                  "a gated shared expert must have the experts' F (a dense branch has no gate)");
     const tsg_expert_offsets& so = d->shared_offsets;
     const uint64_t sb = reinterpret_cast<uintptr_t>(d->shared_expert) | so.gate_w_off |
                         so.gate_s_off | so.up_w_off | so.up_s_off | so.down_w_off | so.down_s_off;
@@ -846,8 +892,32 @@ tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc* d, tsg_mo
   if (!L) return fail(ctx, TSG_ERR_OOM, "layer");
   L->ctx = ctx;
   L->desc = *d;
-  L->has_shared = d->shared_expert ? 1 : 0;
-  L->has_gate = (d->shared_expert && d->shared_gate) ? 1 : 0;
+  if (dense) {
+    // the dense MLP as a one-expert layer that every token takes with weight
+    // 1 (no router of its own); the routed view of the layer has no shared slot
+    tsg_moe_layer_s* Dn = new (std::nothrow) tsg_moe_layer_s();
+    if (!Dn) {
+      delete L;
+      return fail(ctx, TSG_ERR_OOM, "layer");
+    }
+    Dn->ctx = ctx;
+    Dn->desc = *d;
+    Dn->desc.f = d->shared_f;
+    Dn->desc.num_experts = 1;
+    Dn->desc.top_k = 1;
+    Dn->desc.experts = d->shared_expert;
+    Dn->desc.expert_stride = 0;
+    Dn->desc.offsets = d->shared_offsets;
+    Dn->desc.shared_expert = nullptr;
+    Dn->desc.shared_gate = nullptr;
+    Dn->desc.per_expert_scale = nullptr;
+    Dn->desc.logit_bias = nullptr;
+    L->dense = Dn;
+    L->desc.shared_expert = nullptr;
+    L->desc.shared_f = 0;
+  }
+  L->has_shared = L->desc.shared_expert ? 1 : 0;
+  L->has_gate = (L->desc.shared_expert && d->shared_gate) ? 1 : 0;
   const size_t rows = d->num_experts + (L->has_gate ? 1 : 0);
   cudaError_t e = cudaSetDevice(ctx->device);
   if (e == cudaSuccess) e = cudaMalloc(&L->router_rows, rows * d->d * sizeof(float));
@@ -873,6 +943,7 @@ tsg_status tsg_moe_layer_create(tsg_ctx ctx, const tsg_moe_layer_desc* d, tsg_mo
   if (e != cudaSuccess) {
     if (L->router_rows) cudaFree(L->router_rows);
     if (L->router_w3) cudaFree(L->router_w3);
+    delete L->dense;
     delete L;
     return cuda_fail(ctx, e, "layer create");
   }
@@ -886,6 +957,7 @@ tsg_status tsg_moe_layer_destroy(tsg_moe_layer L) {
   // destroyed in either order (cudaFree waits for outstanding work itself)
   if (L->router_rows) cudaFree(L->router_rows);
   if (L->router_w3) cudaFree(L->router_w3);
+  delete L->dense;
   delete L;
   return TSG_OK;
 }
@@ -1185,6 +1257,14 @@ tsg_status tsg_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidde
   if (st != TSG_OK) return st;
   st = ensure_workspace(ctx, layer_caps(L, T));
   if (st != TSG_OK) return st;
+  // the dense branch first (its result becomes the routed pass's residual),
+  // so that the routing left behind for tsg_last_routing is the router's
+  if (L->dense) {
+    st = run_dense_branch(ctx, L, hidden, hidden_stride, T, residual, ctx->dense_y, L->desc.d,
+                          TSG_DTYPE_F32);
+    if (st != TSG_OK) return st;
+    residual = ctx->dense_y;
+  }
   RouterParams p = router_params(L, hidden, hidden_stride, T);
   ctx->last_T = T;
   ctx->last_K = L->desc.top_k;
@@ -1229,6 +1309,16 @@ tsg_status tsg_moe_verify_rows_forward(tsg_ctx ctx, tsg_moe_layer L, const void*
   const size_t K = L->desc.top_k, D = L->desc.d;
   const size_t ysz = y_dtype == TSG_DTYPE_F32 ? 4 : 2;
   prof_mark(ctx, 0);
+  if (L->dense) {
+    // the dense branch row by row, as a one-token block runs it
+    for (uint32_t i = 0; i < T; ++i) {
+      st = run_dense_branch(ctx, L, static_cast<const uint8_t*>(hidden) + static_cast<size_t>(i) * hidden_stride * 2,
+                            hidden_stride, 1, residual ? residual + i * D : nullptr,
+                            ctx->dense_y + i * D, static_cast<uint32_t>(D), TSG_DTYPE_F32);
+      if (st != TSG_OK) return st;
+    }
+    residual = ctx->dense_y;
+  }
   for (uint32_t i = 0; i < T; i += 2) {
     const uint32_t n = T - i < 2 ? T - i : 2;
     st = run_decode_fused(ctx, L, static_cast<const uint8_t*>(hidden) + static_cast<size_t>(i) * hidden_stride * 2,
@@ -1282,6 +1372,11 @@ static tsg_status experts_with_routing(tsg_ctx ctx, tsg_moe_layer L, const void*
   if (decode && T > 64) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "decode regime takes at most 64 tokens");
   st = ensure_workspace(ctx, layer_caps(L, T));
   if (st != TSG_OK) return st;
+  if (L->dense) {
+    st = run_dense_branch(ctx, L, x, x_stride, T, residual, ctx->dense_y, L->desc.d, TSG_DTYPE_F32);
+    if (st != TSG_OK) return st;
+    residual = ctx->dense_y;
+  }
   const size_t P = static_cast<size_t>(T) * L->desc.top_k;
   TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->rb.ids, indices, P * 4, cudaMemcpyDeviceToDevice, ctx->stream),
                "copy ids");
@@ -1340,9 +1435,10 @@ tsg_status tsg_shared_expert(tsg_ctx ctx, tsg_moe_layer L, const void* x, uint32
                              uint32_t T, void* y, uint32_t y_stride, tsg_dtype y_dtype) {
   tsg_status st = check_common(ctx, L, x, x_stride, T, y, y_stride, y_dtype);
   if (st != TSG_OK || T == 0) return st;
-  if (!L->has_shared) return fail(ctx, TSG_ERR_INVALID_ARG, "layer has no shared expert");
+  if (!L->has_shared && !L->dense) return fail(ctx, TSG_ERR_INVALID_ARG, "layer has no shared expert");
   st = ensure_workspace(ctx, layer_caps(L, T));
   if (st != TSG_OK) return st;
+  if (L->dense) return run_dense_branch(ctx, L, x, x_stride, T, nullptr, y, y_stride, y_dtype);
   // a view of the layer with no routed slots: the schedule holds only the
   // shared expert's row tiles
   tsg_moe_layer_s V = *L;
@@ -1478,6 +1574,15 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
   const uint32_t shared_rows = L->has_shared ? T : 0u;
   ctx->last_T = T;
   ctx->last_K = K;
+
+  // 0. the dense branch, local (every rank holds it in full); its result is
+  //    the residual of the routed combine
+  if (L->dense && T > 0) {
+    st = run_dense_branch(ctx, L, hidden, hidden_stride, T, residual, ctx->dense_y, D,
+                          TSG_DTYPE_F32);
+    if (st != TSG_OK) return st;
+    residual = ctx->dense_y;
+  }
 
   // 1. route and group this rank's tokens over all E experts: the sorted
   //    order puts the pairs of each owner rank in one contiguous run

@@ -116,7 +116,9 @@ class MoELayer:
             d.shared_expert = _ptr(t["shared"])
             d.shared_f = t["shared_f"]
             d.shared_offsets = _abi.ExpertOffsets(*t["shared_offsets"])
-            self._sg = t["shared_gate"].float().contiguous()
+            self._sg = t.get("shared_gate")
+            if self._sg is not None:
+                self._sg = self._sg.float().contiguous()
             d.shared_gate = _ptr(self._sg)
         self.desc = d
         h = C.c_void_p()

@@ -27,6 +27,8 @@ CONFIGS = {
     "tiny": (512, 256, 16, 4, 1, 0),
     "gemma": (2816, 704, 128, 8, 0, 0),
     "qwen": (2048, 512, 256, 8, 1, 512),
+    # Gemma-like with its dense MLP branch (a shared int4 MLP of width 2112)
+    "gemma_dense": (2816, 704, 128, 8, 0, 2112),
 }
 
 
@@ -115,7 +117,8 @@ def host_layer(config: str | tuple, seed: int, skew: float | None = None,
         shared = np.zeros(sstride, np.uint8)
         _fill_blob(shared, so, d, shared_f, rng)
         layer.shared, layer.shared_f, layer.shared_offsets = shared, shared_f, so
-        layer.shared_gate = (rng.standard_normal(d) / np.sqrt(d)).astype(np.float32)
+        if shared_f == f:  # a shared expert is gated; a dense branch is not
+            layer.shared_gate = (rng.standard_normal(d) / np.sqrt(d)).astype(np.float32)
     if skew:
         layer.logit_bias = zipf_bias(e, skew, rng)
     return layer
@@ -164,8 +167,9 @@ def device_layer_tensors(config: str | tuple, seed: int, skew: float | None, dev
             n_s = rows * (cols // GROUP)
             sc = (0.01 * torch.randn(n_s, generator=g, device=device).abs() + 1e-3).half()
             sh[s_off:s_off + 2 * n_s] = sc.view(torch.uint8)
-        out.update(shared=sh, shared_f=shared_f, shared_offsets=so,
-                   shared_gate=torch.randn(d, generator=g, device=device) / float(np.sqrt(d)))
+        out.update(shared=sh, shared_f=shared_f, shared_offsets=so)
+        if shared_f == f:  # a shared expert is gated; a dense branch is not
+            out["shared_gate"] = torch.randn(d, generator=g, device=device) / float(np.sqrt(d))
     if skew:
         rng = np.random.default_rng(seed + 0x5EED)
         out["logit_bias"] = torch.from_numpy(zipf_bias(e, skew, rng)).to(device)
@@ -182,7 +186,8 @@ def to_host_layer(t: dict, experts_subset=None) -> HostLayer:
         layer.shared = t["shared"].cpu().numpy()
         layer.shared_f = t["shared_f"]
         layer.shared_offsets = t["shared_offsets"]
-        layer.shared_gate = t["shared_gate"].float().cpu().numpy()
+        if t.get("shared_gate") is not None:
+            layer.shared_gate = t["shared_gate"].float().cpu().numpy()
     if "logit_bias" in t:
         layer.logit_bias = t["logit_bias"].cpu().numpy()
     return layer
