@@ -296,6 +296,23 @@ TSG_API tsg_status tsg_shared_expert(tsg_ctx ctx, tsg_moe_layer layer, const voi
                              uint32_t x_stride, uint32_t T, void *y, uint32_t y_stride,
                              tsg_dtype y_dtype);
 
+/* Import of one int4 projection of a .moepack expert blob
+ * (MoEPackPackedExpertsLayoutV1.swift:3-212; sub-tensors "gate", "gate_scales",
+ * "gate_biases", ... as ModelExpertIO.swift:55-84 reads them) into this
+ * library's expert layout, on the device.  In: codes_u32 [rows][cols/8] U32
+ * words (MLX affine packing), scales_bf16 [rows][cols/group_size] BF16 bits,
+ * biases_bf16 (same shape) or NULL for a `sym` blob.  Out: out_codes
+ * [rows][cols/2] bytes and out_scales_f16 [rows][cols/32] (the layout of
+ * tsg_expert_offsets).  Exact or fails: each BF16 scale must be an fp16 value,
+ * a group of group_size > 32 gives its scale to each of its 32-groups, and
+ * biases when given must be -8 x scale as BF16 bits (MoEPackAffineV1.swift:
+ * 14-26); a failure is reported by tsg_sync as TSG_ERR_METADATA.  Device
+ * pointers; codes 16-byte aligned. */
+TSG_API tsg_status tsg_import_int4_affine(tsg_ctx ctx, const void *codes_u32,
+                                  const uint16_t *scales_bf16, const uint16_t *biases_bf16,
+                                  uint32_t rows, uint32_t cols, uint32_t group_size,
+                                  void *out_codes, uint16_t *out_scales_f16);
+
 /* Stage timing, the analogue of PrefillGPUProfile
  * (Runtime/Prefill/PrefillGPUProfile.swift:1-40): between begin and end,
  * every tsg_moe_block_forward records CUDA events on the context's stream at

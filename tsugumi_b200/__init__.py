@@ -2,10 +2,12 @@
 
 The compute lives in libtsugumi_cuda.so (hand-written CUDA + a C ABI,
 include/tsugumi_cuda.h); this package holds its build script, the ctypes
-bindings, the host-side mirror of the reference's encoder classes, and the
-seeded synthetic-layer generator used by the tests and the benchmark.
+bindings, the host-side mirror of the reference's encoder classes, the
+.moepack packed-experts reader (moepack.py), and the seeded synthetic-layer
+generator used by the tests and the benchmark.
 """
 
+from ._abi import TsgError  # noqa: F401
 from .moe import (  # noqa: F401
     Context,
     MoE,

@@ -100,6 +100,7 @@ SIGNATURES = [
     ("tsg_moe_experts_prefill", _S, [_P, _P, _P, _U, _U, _P, _P, _P, _P, _U, C.c_int]),
     ("tsg_moe_reduce_token_major", _S, [_P, _P, _P, _U, _U, _U, _P, C.c_int]),
     ("tsg_shared_expert", _S, [_P, _P, _P, _U, _U, _P, _U, C.c_int]),
+    ("tsg_import_int4_affine", _S, [_P, _P, _P, _P, _U, _U, _U, _P, _P]),
     ("tsg_ctx_profile_begin", _S, [_P, _U]),
     ("tsg_ctx_profile_end", _S, [_P, C.POINTER(C.c_float), C.POINTER(_U)]),
     ("tsg_last_routing", _S, [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_U),

@@ -579,6 +579,8 @@ const char* grouping_error_text(uint32_t code) {
     case 7: return "route rank %u is out of range";
     case 8: return "route expert %u is out of range";
     case 9: return "duplicate route pair for token %u";
+    case 10: return "imported scale of group %u is not an fp16 value (import is exact or fails)";
+    case 11: return "imported bias of group %u is not -8 x scale (not the symmetric int4 scheme)";
     default: return "routing metadata failed validation (value %u)";
   }
 }
@@ -1329,6 +1331,31 @@ tsg_status tsg_moe_verify_rows_forward(tsg_ctx ctx, tsg_moe_layer L, const void*
     if (st != TSG_OK) return st;
   }
   if (ctx->profiling && ctx->prof_calls < ctx->prof_max) ++ctx->prof_calls;
+  return TSG_OK;
+}
+
+tsg_status tsg_import_int4_affine(tsg_ctx ctx, const void* codes_u32, const uint16_t* scales_bf16,
+                                  const uint16_t* biases_bf16, uint32_t rows, uint32_t cols,
+                                  uint32_t group_size, void* out_codes, uint16_t* out_scales_f16) {
+  if (!ctx || !codes_u32 || !scales_bf16 || !out_codes || !out_scales_f16)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "null argument");
+  if (rows == 0 || cols == 0 || cols % 32)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "columns must be a positive multiple of 32");
+  if (group_size == 0 || group_size % 32 || cols % group_size)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE,
+                "group size must be a multiple of 32 that divides the columns");
+  if (static_cast<uint64_t>(rows) * cols / 2 % 16 ||
+      ((reinterpret_cast<uintptr_t>(codes_u32) | reinterpret_cast<uintptr_t>(out_codes)) & 15u))
+    return fail(ctx, TSG_ERR_INVALID_ARG, "codes must be 16-byte aligned whole vectors");
+  tsg_status st = take_pending_error(ctx);
+  if (st != TSG_OK) return st;
+  TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  TSG_CUDA_TRY(ctx,
+               launch_import_int4(codes_u32, scales_bf16, biases_bf16, static_cast<int>(rows),
+                                  static_cast<int>(cols), static_cast<int>(group_size), out_codes,
+                                  reinterpret_cast<__half*>(out_scales_f16), ctx->status,
+                                  ctx->stream),
+               "import int4");
   return TSG_OK;
 }
 

@@ -245,4 +245,11 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_reduce_token_major(const __half* partials, const float* w, int T, int K, int D,
                                       void* h2, int h2_f32, cudaStream_t s);
 
+// import.cu: one int4 matrix of a .moepack blob (U32 codes, BF16 scales of
+// `group` elements, optional BF16 biases) into codes bytes + fp16 32-group
+// scales, exactly (failures recorded in err: code 10 scale, 11 bias)
+cudaError_t launch_import_int4(const void* codes, const uint16_t* scales, const uint16_t* biases,
+                               int rows, int cols, int group, void* out_codes, __half* out_scales,
+                               uint32_t* err, cudaStream_t s);
+
 }  // namespace tsg
