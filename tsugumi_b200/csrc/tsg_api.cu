@@ -96,8 +96,9 @@ struct tsg_ctx_s {
   __half* ep_out = nullptr;          // local expert outputs [cap][D]
   __half* ep_ret = nullptr;          // returned outputs in this rank's sorted order [cap][D]
   size_t ep_ret_cap = 0;
-  uint32_t* ep_counts_recv = nullptr;  // [world][E / world] (device)
-  uint32_t* ep_h_counts = nullptr;     // pinned: [E] sent counts, then [world][E / world] received
+  uint32_t* ep_counts_recv = nullptr;  // device: [512] received counts, [512] sent counts,
+                                       // [2][world] received status words, [2] own status words
+  uint32_t* ep_h_counts = nullptr;     // pinned: [E] sent counts, [E] received, [world] statuses
   RowTile* ep_tiles = nullptr;         // device row-tile schedule
   RowTile* ep_h_tiles = nullptr;       // pinned staging
   uint32_t* ep_ntiles = nullptr;       // device [1] (follows ep_tiles' capacity)
@@ -604,6 +605,7 @@ struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;  // optional
   ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*group_start)() = nullptr;
@@ -622,6 +624,7 @@ const NcclApi& nccl() {
     api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
     api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
     api.send = reinterpret_cast<decltype(api.send)>(sym("ncclSend"));
     api.recv = reinterpret_cast<decltype(api.recv)>(sym("ncclRecv"));
     api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
@@ -1567,6 +1570,15 @@ tsg_status tsg_ep_init(tsg_ctx ctx, const void* unique_id, int rank, int world) 
   TSG_CUDA_TRY(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
   ncclUniqueId id;
   std::memcpy(&id, unique_id, sizeof(id));
+  // the count and status exchange buffers, allocated here so that a call
+  // never allocates between its collectives
+  if (!ctx->ep_counts_recv) {
+    TSG_CUDA_TRY(ctx, cudaMalloc(&ctx->ep_counts_recv, (1024 + 4 * 1024) * sizeof(uint32_t)),
+                 "cudaMalloc");
+    TSG_CUDA_TRY(ctx, cudaHostAlloc(&ctx->ep_h_counts, (2 * 512 + 1024) * sizeof(uint32_t),
+                                    cudaHostAllocDefault), "cudaHostAlloc");
+  }
+  if (world > 1024) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "at most 1024 ranks");
   ncclComm_t comm = nullptr;
   TSG_NCCL_TRY(ctx, n.comm_init_rank(&comm, world, id, rank), "ncclCommInitRank");
   ctx->nccl_comm = comm;
@@ -1575,81 +1587,158 @@ tsg_status tsg_ep_init(tsg_ctx ctx, const void* unique_id, int rank, int world) 
   return TSG_OK;
 }
 
+// Every rank of the group takes the same collective steps in the same order,
+// whatever fails where: a local failure (bad arguments, a launch, an
+// allocation, the pair counts) is carried to the peers in a status word at
+// the next of two agreement points -- beside the count exchange, and after
+// the plan and its allocations -- and then every rank returns together,
+// before any further collective.  Past the second point nothing allocates;
+// a CUDA failure there is reported after the return exchange, and an NCCL
+// failure aborts the communicator (the group must be built again).
 tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t expert_first,
                                     const void* hidden, uint32_t hidden_stride, uint32_t T,
                                     const float* residual, void* y, uint32_t y_stride,
                                     tsg_dtype y_dtype) {
-  tsg_status st = check_common(ctx, L, hidden, hidden_stride, T, y, y_stride, y_dtype);
-  if (st != TSG_OK) return st;
+  if (!ctx || !L) return fail(ctx, TSG_ERR_INVALID_ARG, "null context or layer");
   if (!ctx->nccl_comm) return fail(ctx, TSG_ERR_INVALID_ARG, "tsg_ep_init has not been called");
   const int R = ctx->ep_world, rank = ctx->ep_rank;
   const uint32_t E = L->desc.num_experts, K = L->desc.top_k, D = L->desc.d, F = L->desc.f;
-  if (E % static_cast<uint32_t>(R))
-    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "numExperts must be a multiple of the group size");
-  const uint32_t El = E / static_cast<uint32_t>(R);
-  if (expert_first != static_cast<uint32_t>(rank) * El)
-    return fail(ctx, TSG_ERR_INVALID_ARG, "expert_first must be rank * numExperts / world");
-  st = take_pending_error(ctx);
-  if (st != TSG_OK) return st;
-  st = ensure_workspace(ctx, layer_caps(L, std::max<uint32_t>(T, 1)));
-  if (st != TSG_OK) return st;
   const NcclApi& n = nccl();
   ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
   cudaStream_t s = ctx->stream;
   RouteBuffers& rb = ctx->rb;
+  const uint32_t El = E % static_cast<uint32_t>(R) ? 0u : E / static_cast<uint32_t>(R);
   const uint32_t P = T * K;
   const uint32_t shared_rows = L->has_shared ? T : 0u;
-  ctx->last_T = T;
-  ctx->last_K = K;
+  uint32_t* counts_recv = ctx->ep_counts_recv;      // [512]
+  uint32_t* counts_send = ctx->ep_counts_recv + 512;  // [512]
+  uint32_t* status_recv = ctx->ep_counts_recv + 1024;  // [2][1024]
+  uint32_t* status_send = ctx->ep_counts_recv + 1024 + 2048;  // [2]
+  uint32_t* hc = ctx->ep_h_counts;  // [E] sent, [E] received, [R] statuses
 
-  // 0. the dense branch, local (every rank holds it in full); its result is
-  //    the residual of the routed combine
-  if (L->dense && T > 0) {
-    st = run_dense_branch(ctx, L, hidden, hidden_stride, T, residual, ctx->dense_y, D,
-                          TSG_DTYPE_F32);
-    if (st != TSG_OK) return st;
+  // an NCCL failure leaves the group in no known state: abort it
+  auto nccl_abort = [&](ncclResult_t r, const char* where) {
+    if (n.comm_abort) n.comm_abort(comm);
+    else n.comm_destroy(comm);
+    ctx->nccl_comm = nullptr;
+    return nccl_fail(ctx, r, where);
+  };
+#define EP_NCCL(expr, where)                                  \
+  do {                                                        \
+    const ncclResult_t r__ = (expr);                          \
+    if (r__ != ncclSuccess) return nccl_abort(r__, where);    \
+  } while (0)
+  // agreement: every rank sends its status word to every peer; true when
+  // every rank (this one included) is fine
+  auto agree = [&](int round, bool ok_local) -> tsg_status {
+    if (cudaMemsetAsync(status_send + round, ok_local ? 1 : 0, 4, s) != cudaSuccess) ok_local = false;
+    EP_NCCL(n.group_start(), "ncclGroupStart");
+    for (int q = 0; q < R; ++q) {
+      EP_NCCL(n.send(status_send + round, 1, ncclUint32, q, comm, s), "ncclSend(status)");
+      EP_NCCL(n.recv(status_recv + round * 1024 + q, 1, ncclUint32, q, comm, s),
+              "ncclRecv(status)");
+    }
+    EP_NCCL(n.group_end(), "ncclGroupEnd");
+    return TSG_OK;
+  };
+  auto read_statuses = [&](int round, bool* all_ok, int* first_bad) -> tsg_status {
+    if (cudaMemcpyAsync(hc + 2 * 512, status_recv + round * 1024, R * 4u,
+                        cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return fail(ctx, TSG_ERR_CUDA, "expert-parallel: status readback");
+    *all_ok = true;
+    for (int q = 0; q < R; ++q)
+      if (hc[2 * 512 + q] == 0u) {
+        *all_ok = false;
+        if (*first_bad < 0) *first_bad = q;
+      }
+    return TSG_OK;
+  };
+
+  // ---- phase 1 (local): checks, routing, sorting, the rows to send ----
+  tsg_status local = TSG_OK;
+  std::string local_msg;
+  auto note = [&](tsg_status st) {
+    if (local == TSG_OK && st != TSG_OK) {
+      local = st;
+      local_msg = ctx->last_error;
+    }
+  };
+  note(check_common(ctx, L, hidden, hidden_stride, T, y, y_stride, y_dtype));
+  if (local == TSG_OK && El == 0)
+    note(fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "numExperts must be a multiple of the group size"));
+  if (local == TSG_OK && expert_first != static_cast<uint32_t>(rank) * El)
+    note(fail(ctx, TSG_ERR_INVALID_ARG, "expert_first must be rank * numExperts / world"));
+  if (local == TSG_OK) note(take_pending_error(ctx));
+  if (local == TSG_OK) note(ensure_workspace(ctx, layer_caps(L, std::max<uint32_t>(T, 1))));
+  if (local == TSG_OK) {
+    ctx->last_T = T;
+    ctx->last_K = K;
+  }
+  // the dense branch, local (every rank holds it in full); its result is the
+  // residual of the routed combine
+  if (local == TSG_OK && L->dense && T > 0) {
+    note(run_dense_branch(ctx, L, hidden, hidden_stride, T, residual, ctx->dense_y, D,
+                          TSG_DTYPE_F32));
     residual = ctx->dense_y;
   }
+  // route and group this rank's tokens over all E experts: the sorted order
+  // puts the pairs of each owner rank in one contiguous run
+  auto route = [&]() -> tsg_status {
+    if (T > 0) {
+      const RouterParams p = router_params(L, hidden, hidden_stride, T);
+      TSG_CUDA_TRY(ctx, launch_router_prefill(p, rb, s), "router");
+      TSG_CUDA_TRY(ctx, launch_permute(p, rb, nullptr, s), "permute");
+      const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(E) * D : nullptr;
+      TSG_CUDA_TRY(ctx,
+                   launch_gather_rows_gate(static_cast<const uint16_t*>(hidden), hidden_stride,
+                                           rb.inv_rms, rb.sorted_pairs, static_cast<int>(P),
+                                           static_cast<int>(T), static_cast<int>(D), L->has_shared,
+                                           ctx->xp, gate_w, rb.gate_raw, s),
+                   "gather rows");
+      TSG_CUDA_TRY(ctx, cudaMemcpyAsync(counts_send, rb.counts, E * 4u, cudaMemcpyDeviceToDevice, s),
+                   "counts");
+    } else {
+      TSG_CUDA_TRY(ctx, cudaMemsetAsync(counts_send, 0, E * 4u, s), "memset");
+    }
+    return TSG_OK;
+  };
+  if (local == TSG_OK) note(route());
+  if (local != TSG_OK) cudaMemsetAsync(counts_send, 0, 512 * 4u, s);  // (what is sent is not read)
 
-  // 1. route and group this rank's tokens over all E experts: the sorted
-  //    order puts the pairs of each owner rank in one contiguous run
-  if (T > 0) {
-    const RouterParams p = router_params(L, hidden, hidden_stride, T);
-    TSG_CUDA_TRY(ctx, launch_router_prefill(p, rb, s), "router");
-    TSG_CUDA_TRY(ctx, launch_permute(p, rb, nullptr, s), "permute");
-    const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(E) * D : nullptr;
-    TSG_CUDA_TRY(ctx,
-                 launch_gather_rows_gate(static_cast<const uint16_t*>(hidden), hidden_stride,
-                                         rb.inv_rms, rb.sorted_pairs, static_cast<int>(P),
-                                         static_cast<int>(T), static_cast<int>(D), L->has_shared,
-                                         ctx->xp, gate_w, rb.gate_raw, s),
-                 "gather rows");
-  } else {
-    TSG_CUDA_TRY(ctx, cudaMemsetAsync(rb.counts, 0, E * 4u, s), "memset");
+  // ---- agreement 1, with the per-expert pair counts to their owners ----
+  const uint32_t Elx = El ? El : E / static_cast<uint32_t>(R);  // counts each peer expects
+  {
+    bool ok_local = local == TSG_OK;
+    if (cudaMemsetAsync(status_send, ok_local ? 1 : 0, 4, s) != cudaSuccess) ok_local = false;
+    EP_NCCL(n.group_start(), "ncclGroupStart");
+    for (int q = 0; q < R; ++q) {
+      if (Elx) {
+        EP_NCCL(n.send(counts_send + q * Elx, Elx, ncclUint32, q, comm, s), "ncclSend(counts)");
+        EP_NCCL(n.recv(counts_recv + q * Elx, Elx, ncclUint32, q, comm, s), "ncclRecv(counts)");
+      }
+      EP_NCCL(n.send(status_send, 1, ncclUint32, q, comm, s), "ncclSend(status)");
+      EP_NCCL(n.recv(status_recv + q, 1, ncclUint32, q, comm, s), "ncclRecv(status)");
+    }
+    EP_NCCL(n.group_end(), "ncclGroupEnd");
   }
+  bool all_ok = false;
+  int first_bad = -1;
+  if (cudaMemcpyAsync(hc, counts_send, E * 4u, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemcpyAsync(hc + E, counts_recv, E * 4u, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: counts readback"));
+  {
+    const tsg_status st = read_statuses(0, &all_ok, &first_bad);
+    if (st != TSG_OK) return nccl_abort(ncclSystemError, "expert-parallel status readback");
+  }
+  if (local != TSG_OK) return fail(ctx, local, local_msg);
+  if (!all_ok)
+    return fail(ctx, TSG_ERR_NCCL, "expert-parallel: rank " + std::to_string(first_bad) +
+                                       " failed before the row exchange (its own call reports why)");
 
-  // 2. per-expert pair counts to the experts' owners; the host needs them
-  //    to size the row exchange
-  if (!ctx->ep_counts_recv) {
-    TSG_CUDA_TRY(ctx, cudaMalloc(&ctx->ep_counts_recv, 512 * sizeof(uint32_t)), "cudaMalloc");
-    TSG_CUDA_TRY(ctx, cudaHostAlloc(&ctx->ep_h_counts, 2 * 512 * sizeof(uint32_t),
-                                    cudaHostAllocDefault), "cudaHostAlloc");
-  }
-  TSG_NCCL_TRY(ctx, n.group_start(), "ncclGroupStart");
-  for (int q = 0; q < R; ++q) {
-    TSG_NCCL_TRY(ctx, n.send(rb.counts + q * El, El, ncclUint32, q, comm, s), "ncclSend(counts)");
-    TSG_NCCL_TRY(ctx, n.recv(ctx->ep_counts_recv + q * El, El, ncclUint32, q, comm, s),
-                 "ncclRecv(counts)");
-  }
-  TSG_NCCL_TRY(ctx, n.group_end(), "ncclGroupEnd");
-  uint32_t* hc = ctx->ep_h_counts;
-  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(hc, rb.counts, E * 4u, cudaMemcpyDeviceToHost, s), "counts");
-  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(hc + E, ctx->ep_counts_recv, E * 4u, cudaMemcpyDeviceToHost, s),
-               "counts");
-  TSG_CUDA_TRY(ctx, cudaStreamSynchronize(s), "cudaStreamSynchronize");
-
-  // 3. the plan: send/receive runs per peer, and the local row tiles -- one
-  //    run per (source rank, local expert), then the shared expert's rows
+  // ---- phase 2 (local): the plan and its buffers ----
+  // send/receive runs per peer, and the local row tiles -- one run per
+  // (source rank, local expert), then the shared expert's rows
   std::vector<uint32_t> send_cnt(R), send_off(R), recv_cnt(R), recv_off(R);
   uint32_t so = 0, ro = 0;
   for (int q = 0; q < R; ++q) {
@@ -1665,7 +1754,7 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
     so += sc;
     ro += rc;
   }
-  if (so != P) return fail(ctx, TSG_ERR_CUDA, "expert-parallel: pair counts do not add up");
+  if (so != P) note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: pair counts do not add up"));
   const uint32_t recv_rows = ro;
   const uint32_t rows_local = recv_rows + shared_rows;
   const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
@@ -1681,60 +1770,83 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
   for (uint32_t b = 0; b < shared_rows; b += tr)
     tiles.push_back({El, recv_rows + b, std::min(tr, shared_rows - b), 0});
   const uint32_t n_tiles = static_cast<uint32_t>(tiles.size());
+  auto buffers = [&]() -> tsg_status {
+    // (the stream is idle here, so buffers can be replaced)
+    if (rows_local > ctx->ep_rows_cap || static_cast<size_t>(D) * ctx->ep_rows_cap == 0) {
+      const size_t rows = std::max<size_t>(rows_local + rows_local / 4, 1024);
+      size_t c1 = 0, c2 = 0, c3 = 0;
+      ctx->ep_rows_cap = 0;
+      TSG_CUDA_TRY(ctx, grow(&ctx->ep_rows, &c1, rows * D), "cudaMalloc");
+      TSG_CUDA_TRY(ctx, grow(&ctx->ep_act, &c2, rows * F), "cudaMalloc");
+      TSG_CUDA_TRY(ctx, grow(&ctx->ep_out, &c3, rows * D), "cudaMalloc");
+      ctx->ep_rows_cap = rows;
+    }
+    TSG_CUDA_TRY(ctx, grow(&ctx->ep_ret, &ctx->ep_ret_cap, static_cast<size_t>(P + shared_rows) * D),
+                 "cudaMalloc");
+    if (!ctx->ep_tiles || ctx->ep_tiles_cap < n_tiles + 1) {
+      if (ctx->ep_tiles) cudaFree(ctx->ep_tiles);
+      if (ctx->ep_h_tiles) cudaFreeHost(ctx->ep_h_tiles);
+      ctx->ep_tiles = nullptr;
+      ctx->ep_h_tiles = nullptr;
+      ctx->ep_tiles_cap = 0;
+      const size_t cap = std::max<size_t>(2 * (n_tiles + 1), 256);
+      TSG_CUDA_TRY(ctx, cudaMalloc(&ctx->ep_tiles, (cap + 1) * sizeof(RowTile)), "cudaMalloc");
+      TSG_CUDA_TRY(ctx, cudaHostAlloc(&ctx->ep_h_tiles, (cap + 1) * sizeof(RowTile),
+                                      cudaHostAllocDefault), "cudaHostAlloc");
+      ctx->ep_tiles_cap = cap;
+    }
+    // the tile count rides in the slot after the tiles
+    RowTile* ht = ctx->ep_h_tiles;
+    std::copy(tiles.begin(), tiles.end(), ht);
+    ht[ctx->ep_tiles_cap].expert = n_tiles;
+    ctx->ep_ntiles = &ctx->ep_tiles[ctx->ep_tiles_cap].expert;
+    if (n_tiles)
+      TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_tiles, ht, n_tiles * sizeof(RowTile),
+                                        cudaMemcpyHostToDevice, s), "tiles");
+    TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_ntiles, &ht[ctx->ep_tiles_cap].expert,
+                                      sizeof(uint32_t), cudaMemcpyHostToDevice, s), "tiles");
+    return TSG_OK;
+  };
+  if (local == TSG_OK) note(buffers());
 
-  // (the stream is idle here, so buffers can be replaced)
-  if (rows_local > ctx->ep_rows_cap || static_cast<size_t>(D) * ctx->ep_rows_cap == 0) {
-    const size_t rows = std::max<size_t>(rows_local + rows_local / 4, 1024);
-    size_t c1 = 0, c2 = 0, c3 = 0;
-    ctx->ep_rows_cap = 0;
-    TSG_CUDA_TRY(ctx, grow(&ctx->ep_rows, &c1, rows * D), "cudaMalloc");
-    TSG_CUDA_TRY(ctx, grow(&ctx->ep_act, &c2, rows * F), "cudaMalloc");
-    TSG_CUDA_TRY(ctx, grow(&ctx->ep_out, &c3, rows * D), "cudaMalloc");
-    ctx->ep_rows_cap = rows;
+  // ---- agreement 2: every rank's plan and buffers are in place ----
+  {
+    const tsg_status st = agree(1, local == TSG_OK);
+    if (st != TSG_OK) return st;
   }
-  TSG_CUDA_TRY(ctx, grow(&ctx->ep_ret, &ctx->ep_ret_cap, static_cast<size_t>(P + shared_rows) * D),
-               "cudaMalloc");
-  if (!ctx->ep_tiles || ctx->ep_tiles_cap < n_tiles + 1) {
-    if (ctx->ep_tiles) cudaFree(ctx->ep_tiles);
-    if (ctx->ep_h_tiles) cudaFreeHost(ctx->ep_h_tiles);
-    ctx->ep_tiles = nullptr;
-    ctx->ep_h_tiles = nullptr;
-    const size_t cap = std::max<size_t>(2 * (n_tiles + 1), 256);
-    TSG_CUDA_TRY(ctx, cudaMalloc(&ctx->ep_tiles, (cap + 1) * sizeof(RowTile)), "cudaMalloc");
-    TSG_CUDA_TRY(ctx, cudaHostAlloc(&ctx->ep_h_tiles, (cap + 1) * sizeof(RowTile),
-                                    cudaHostAllocDefault), "cudaHostAlloc");
-    ctx->ep_tiles_cap = cap;
+  first_bad = -1;
+  {
+    const tsg_status st = read_statuses(1, &all_ok, &first_bad);
+    if (st != TSG_OK) return nccl_abort(ncclSystemError, "expert-parallel status readback");
   }
-  // the tile count rides in the slot after the tiles
-  RowTile* ht = ctx->ep_h_tiles;
-  std::copy(tiles.begin(), tiles.end(), ht);
-  ht[ctx->ep_tiles_cap].expert = n_tiles;
-  ctx->ep_ntiles = &ctx->ep_tiles[ctx->ep_tiles_cap].expert;
-  if (n_tiles)
-    TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_tiles, ht, n_tiles * sizeof(RowTile),
-                                      cudaMemcpyHostToDevice, s), "tiles");
-  TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_ntiles, &ht[ctx->ep_tiles_cap].expert, sizeof(uint32_t),
-                                    cudaMemcpyHostToDevice, s), "tiles");
+  if (local != TSG_OK) return fail(ctx, local, local_msg);
+  if (!all_ok)
+    return fail(ctx, TSG_ERR_NCCL, "expert-parallel: rank " + std::to_string(first_bad) +
+                                       " failed before the row exchange (its own call reports why)");
 
-  // 4. dispatch: each owner receives its rows, run after run
+  // ---- phase 3: dispatch, contraction, return, combine (no allocation; a
+  // CUDA failure is reported after the return exchange) ----
+  auto cuda_note = [&](cudaError_t e, const char* where) {
+    if (e != cudaSuccess) note(cuda_fail(ctx, e, where));
+  };
   const size_t rowb = D;  // elements per row
-  TSG_NCCL_TRY(ctx, n.group_start(), "ncclGroupStart");
+  EP_NCCL(n.group_start(), "ncclGroupStart");
   for (int q = 0; q < R; ++q) {
     if (send_cnt[q])
-      TSG_NCCL_TRY(ctx, n.send(ctx->xp + send_off[q] * rowb, send_cnt[q] * rowb, ncclFloat16, q,
-                               comm, s), "ncclSend(rows)");
+      EP_NCCL(n.send(ctx->xp + send_off[q] * rowb, send_cnt[q] * rowb, ncclFloat16, q, comm, s),
+              "ncclSend(rows)");
     if (recv_cnt[q])
-      TSG_NCCL_TRY(ctx, n.recv(ctx->ep_rows + recv_off[q] * rowb, recv_cnt[q] * rowb, ncclFloat16,
-                               q, comm, s), "ncclRecv(rows)");
+      EP_NCCL(n.recv(ctx->ep_rows + recv_off[q] * rowb, recv_cnt[q] * rowb, ncclFloat16, q, comm,
+                     s),
+              "ncclRecv(rows)");
   }
-  TSG_NCCL_TRY(ctx, n.group_end(), "ncclGroupEnd");
+  EP_NCCL(n.group_end(), "ncclGroupEnd");
   if (shared_rows)
-    TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_rows + recv_rows * rowb, ctx->xp + P * rowb,
-                                      shared_rows * rowb * 2, cudaMemcpyDeviceToDevice, s),
-                 "shared rows");
-
-  // 5. the grouped contraction over the rows this rank holds
-  if (n_tiles) {
+    cuda_note(cudaMemcpyAsync(ctx->ep_rows + recv_rows * rowb, ctx->xp + P * rowb,
+                              shared_rows * rowb * 2, cudaMemcpyDeviceToDevice, s),
+              "shared rows");
+  // the grouped contraction over the rows this rank holds
+  if (n_tiles && local == TSG_OK) {
     QmmParams qp{};
     qp.D = static_cast<int>(D);
     qp.F = static_cast<int>(F);
@@ -1749,27 +1861,30 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
     qp.partials = ctx->ep_out;
     qp.err = rb.err;
     qp.num_sms = ctx->num_sms;
-    TSG_CUDA_TRY(ctx, launch_qmm_gate_up(qp, s), "qmm gate/up");
-    TSG_CUDA_TRY(ctx, launch_qmm_down(qp, s), "qmm down");
+    cuda_note(launch_qmm_gate_up(qp, s), "qmm gate/up");
+    if (local == TSG_OK) cuda_note(launch_qmm_down(qp, s), "qmm down");
   }
-
-  // 6. return the outputs to the tokens' ranks, into their sorted positions
-  TSG_NCCL_TRY(ctx, n.group_start(), "ncclGroupStart");
+  // return the outputs to the tokens' ranks, into their sorted positions
+  EP_NCCL(n.group_start(), "ncclGroupStart");
   for (int q = 0; q < R; ++q) {
     if (recv_cnt[q])
-      TSG_NCCL_TRY(ctx, n.send(ctx->ep_out + recv_off[q] * rowb, recv_cnt[q] * rowb, ncclFloat16,
-                               q, comm, s), "ncclSend(outputs)");
+      EP_NCCL(n.send(ctx->ep_out + recv_off[q] * rowb, recv_cnt[q] * rowb, ncclFloat16, q, comm,
+                     s),
+              "ncclSend(outputs)");
     if (send_cnt[q])
-      TSG_NCCL_TRY(ctx, n.recv(ctx->ep_ret + send_off[q] * rowb, send_cnt[q] * rowb, ncclFloat16,
-                               q, comm, s), "ncclRecv(outputs)");
+      EP_NCCL(n.recv(ctx->ep_ret + send_off[q] * rowb, send_cnt[q] * rowb, ncclFloat16, q, comm,
+                     s),
+              "ncclRecv(outputs)");
   }
-  TSG_NCCL_TRY(ctx, n.group_end(), "ncclGroupEnd");
+  EP_NCCL(n.group_end(), "ncclGroupEnd");
+#undef EP_NCCL
+  if (local != TSG_OK) return fail(ctx, local, local_msg);
   if (shared_rows)
     TSG_CUDA_TRY(ctx, cudaMemcpyAsync(ctx->ep_ret + P * rowb, ctx->ep_out + recv_rows * rowb,
                                       shared_rows * rowb * 2, cudaMemcpyDeviceToDevice, s),
                  "shared outputs");
 
-  // 7. combine this rank's tokens, ranks in order (as on one GPU)
+  // combine this rank's tokens, ranks in order (as on one GPU)
   if (T > 0) {
     CombineParams cp{};
     cp.T = static_cast<int>(T);
