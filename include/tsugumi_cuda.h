@@ -296,6 +296,36 @@ TSG_API tsg_status tsg_shared_expert(tsg_ctx ctx, tsg_moe_layer layer, const voi
                              uint32_t x_stride, uint32_t T, void *y, uint32_t y_stride,
                              tsg_dtype y_dtype);
 
+/* The norm weights around Gemma's MoE block (BF16 [D] each; RMSNorm is
+ * x * rsqrt(mean(x^2) + eps) * w), as fused_post_attn_setup and
+ * fused_layer_tail (fused.metal:190-374) and the dense branch's post-norm
+ * (RealForwardRunner.swift:3236-3242) take them. */
+typedef struct {
+    const uint16_t *post_attn;    /* norm of the attention output */
+    const uint16_t *pre_ffn;      /* the dense branch's input norm */
+    const uint16_t *pre_ffn2;     /* the routed experts' input norm */
+    const uint16_t *post_dense;   /* the dense branch's output norm */
+    const uint16_t *post_routed;  /* the routed output's norm */
+    const uint16_t *post_ffn;     /* the summed branches' norm */
+    float eps;
+    float layer_scalar;
+} tsg_gemma_norms;
+
+/* Gemma's layer FFN with the adjacent norms and residuals fused, per token
+ * (bf16 activations, rounded where the reference rounds to fp16):
+ *   h       = hidden + norm(attn, post_attn)          (hidden updated)
+ *   x^      = h * rsqrt(mean(h^2) + eps)
+ *   d       = norm(dense(x^ * pre_ffn), post_dense)     (the dense branch)
+ *   r       = norm(moe(route: x^, experts: x^ * pre_ffn2), post_routed)
+ *   hidden  = (h + norm(d + r, post_ffn)) * layer_scalar
+ * Replaces fused_post_attn_setup / fused_layer_tail (fused.metal:190-374)
+ * and the sequence around them in RealForwardRunner.swift:3079-3330.  The
+ * layer is created with router_norm = 0 and a dense branch
+ * (shared_f != f; without one d = 0). */
+TSG_API tsg_status tsg_gemma_ffn_forward(tsg_ctx ctx, tsg_moe_layer layer, const tsg_gemma_norms *norms,
+                                 void *hidden_bf16, uint32_t hidden_stride,
+                                 const void *attn_bf16, uint32_t attn_stride, uint32_t T);
+
 /* Import of one int4 projection of a .moepack expert blob
  * (MoEPackPackedExpertsLayoutV1.swift:3-212; sub-tensors "gate", "gate_scales",
  * "gate_biases", ... as ModelExpertIO.swift:55-84 reads them) into this

@@ -26,6 +26,9 @@ ties unordered, so tests exclude near-ties).
 The block input is the no-scale RMSNorm of the bf16 hidden rows when the
 layer asks for it (rmsnorm.metal:154-175), computed in fp64 and rounded to
 fp32, as tests/golden/make_golden.py does for the reference's own ``_moe``.
+
+``gemma_ffn`` restates Gemma's layer FFN with the norms and residuals the
+reference fuses around the block (fused.metal:190-374).
 """
 
 from __future__ import annotations
@@ -127,3 +130,59 @@ def moe_block(layer, x_bf16: np.ndarray, ids: np.ndarray | None = None,
             sh = sigmoid(xn @ layer.shared_gate.astype(np.float32))[:, None] * sh
         y = y + sh
     return y.astype(np.float32)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 -> fp32, round to nearest even."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    return b.astype(np.uint32).view(np.float32)
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, np.uint32) << 16).view(np.float32)
+
+
+def _inv_rms(x: np.ndarray, eps: float) -> np.ndarray:
+    x64 = x.astype(np.float64)
+    return (1.0 / np.sqrt(np.mean(x64 * x64, axis=1, keepdims=True) + eps)).astype(np.float32)
+
+
+def gemma_ffn(layer, norms: dict, hidden_bf16: np.ndarray, attn_bf16: np.ndarray,
+              eps: float, layer_scalar: float) -> np.ndarray:
+    """Gemma's layer FFN with the adjacent norms: fused_post_attn_setup and
+    fused_layer_tail (Sources/Tsugumi/Metal/Fusions/fused.metal:190-267,
+    :269-374) around the dense branch (SharedExpertInt4.swift:30-94, then
+    its post-norm, RealForwardRunner.swift:3236-3242) and the routed block
+    (routed on the normalised row, experts on it times pre_ffn2).  RMSNorm is
+    x * rsqrt(mean(x^2) + eps) * w; every stored intermediate is rounded to
+    bf16 where the reference rounds to fp16.  `norms` holds bf16 bit arrays
+    [D]; `layer` is a HostLayer whose shared blob is the dense branch.
+    Returns the new hidden rows (fp32 values, bf16-representable)."""
+    import copy
+
+    w = {k: bf16_bits_to_f32(v)[None, :] for k, v in norms.items()}
+    h0 = bf16_bits_to_f32(hidden_bf16)
+    a = bf16_bits_to_f32(attn_bf16)
+    a_n = bf16_round(a * _inv_rms(a, eps) * w["post_attn"])
+    h = bf16_round(h0 + a_n)
+    xh = h * _inv_rms(h, eps)
+    router_x = bf16_round(xh)
+    routed_x = bf16_round(xh * w["pre_ffn2"])
+    dense_x = bf16_round(xh * w["pre_ffn"])
+    routed = copy.copy(layer)
+    routed.router_norm = False
+    routed.shared = None
+    to_bits = lambda v: (v.view(np.uint32) >> 16).astype(np.uint16)  # noqa: E731
+    ids, weights, _ = route(routed, router_x)
+    h2 = moe_block(routed, to_bits(routed_x), ids, weights)
+    r = bf16_round(h2 * _inv_rms(h2, eps) * w["post_routed"])
+    if layer.shared is not None:
+        h1 = ffn(layer.shared, layer.shared_offsets, layer.d, layer.shared_f, dense_x, layer.act)
+        d1 = bf16_round(h1.astype(np.float32) * _inv_rms(h1, eps) * w["post_dense"])
+    else:
+        d1 = np.zeros_like(r)
+    h12 = bf16_round(d1 + r)
+    f = bf16_round(h12 * _inv_rms(h12, eps) * w["post_ffn"])
+    scale = bf16_round(np.array([layer_scalar], np.float32))[0]
+    return bf16_round(bf16_round(h + f) * scale), h

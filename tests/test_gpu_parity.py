@@ -476,3 +476,44 @@ def test_verify_rows_bit_equal_to_decode(ctx, name, T):
     assert np.array_equal(ids.cpu().numpy().astype(np.uint32)[ok], ref_ids[ok])
     y_ref, _, _ = ol.block(x, ids.cpu().numpy().astype(np.uint32), w.cpu().numpy())
     assert rel_l2(y0.cpu().numpy(), y_ref) <= REL_L2
+
+
+@pytest.mark.parametrize("T,scalar", [(1, 1.0), (3, 0.5), (40, 1.0)])
+def test_gemma_fused_norms_match_oracle(ctx, T, scalar):
+    """Gemma's layer FFN with the adjacent norms and residuals fused
+    (fused_post_attn_setup / fused_layer_tail, fused.metal:190-374) against
+    the oracle's restatement: the new hidden rows, and the FFN's part of
+    them (the new rows less the post-attention residual), over the fused
+    decode kernel (T <= 4) and the batched GEMVs (T = 40)."""
+    from oracle import numpy_moe as N
+
+    key = ("gemma_dense_nonorm", 11)
+    if key not in _LAYERS:
+        host = host_layer("gemma_dense", 11)
+        host.router_norm = False
+        dev = tb.MoELayer(ctx, tb.upload_host_layer(host), router_norm=False)
+        _LAYERS[key] = (host, dev, None)
+    host, dev, _ = _LAYERS[key]
+    rng = np.random.default_rng(40 + T)
+    hidden = host_tokens(T, host.d, 60 + T)
+    attn = host_tokens(T, host.d, 61 + T)
+    from tsugumi_b200.synthetic import f32_to_bf16_bits
+
+    names = ("post_attn", "pre_ffn", "pre_ffn2", "post_dense", "post_routed", "post_ffn")
+    norms = {k: f32_to_bf16_bits(1.0 + 0.2 * rng.standard_normal(host.d).astype(np.float32))
+             for k in names}
+    want, h_ref = N.gemma_ffn(host, norms, hidden, attn, 1e-6, scalar)
+    hd = to_dev(hidden)
+    ad = to_dev(attn)
+    nd = {k: torch.from_numpy(v.view(np.int16)).cuda().view(torch.bfloat16) for k, v in norms.items()}
+    with regime(ctx, 4, True):
+        dev.gemma_ffn(hd, ad, nd, eps=1e-6, layer_scalar=scalar)
+        ctx.sync()
+    got = hd.float().cpu().numpy()
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, want) <= 1e-2
+    # the FFN's part alone (the new rows less the post-attention residual)
+    d_got, d_want = got / scalar - h_ref, want / scalar - h_ref
+    err = rel_l2(d_got, d_want)
+    print(f"gemma fused T={T}: rel L2 of the FFN part {err:.3e}")
+    assert err <= 3e-2

@@ -66,6 +66,12 @@ class LayerDesc(C.Structure):
 
 
 # (name, restype, argtypes) for every symbol the header declares.
+class GemmaNorms(C.Structure):
+    _fields_ = [("post_attn", C.c_void_p), ("pre_ffn", C.c_void_p), ("pre_ffn2", C.c_void_p),
+                ("post_dense", C.c_void_p), ("post_routed", C.c_void_p),
+                ("post_ffn", C.c_void_p), ("eps", C.c_float), ("layer_scalar", C.c_float)]
+
+
 _P = C.c_void_p
 _U = C.c_uint32
 _I = C.c_int32
@@ -101,6 +107,7 @@ SIGNATURES = [
     ("tsg_moe_reduce_token_major", _S, [_P, _P, _P, _U, _U, _U, _P, C.c_int]),
     ("tsg_shared_expert", _S, [_P, _P, _P, _U, _U, _P, _U, C.c_int]),
     ("tsg_import_int4_affine", _S, [_P, _P, _P, _P, _U, _U, _U, _P, _P]),
+    ("tsg_gemma_ffn_forward", _S, [_P, _P, C.POINTER(GemmaNorms), _P, _U, _P, _U, _U]),
     ("tsg_ctx_profile_begin", _S, [_P, _U]),
     ("tsg_ctx_profile_end", _S, [_P, C.POINTER(C.c_float), C.POINTER(_U)]),
     ("tsg_last_routing", _S, [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_U),

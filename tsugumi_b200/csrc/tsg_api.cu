@@ -31,8 +31,10 @@ namespace {
 struct Caps {
   uint32_t T = 0, D = 0, F = 0, E = 0, K = 0;
   uint32_t dense = 0;  // 1: a layer with a dense branch (its routed result is staged in f32)
+  uint32_t fusion = 0;  // 1: the Gemma fused entry's block inputs and branch outputs
   bool covers(const Caps& o) const {
-    return T >= o.T && D >= o.D && F >= o.F && E >= o.E && K >= o.K && dense >= o.dense;
+    return T >= o.T && D >= o.D && F >= o.F && E >= o.E && K >= o.K && dense >= o.dense &&
+           fusion >= o.fusion;
   }
   Caps max_with(const Caps& o) const {
     Caps c;
@@ -42,6 +44,7 @@ struct Caps {
     c.E = std::max(E, o.E);
     c.K = std::max(K, o.K);
     c.dense = std::max(dense, o.dense);
+    c.fusion = std::max(fusion, o.fusion);
     return c;
   }
 };
@@ -66,6 +69,10 @@ struct tsg_ctx_s {
   __half* xp = nullptr;
   __half* partials = nullptr;
   float* dense_y = nullptr;  // [T][D] f32: a dense-branch layer's routed result
+  // the Gemma fused entry: [T][D] bf16 router, routed and dense inputs; [T][D]
+  // f32 routed and dense outputs
+  uint16_t* fx_in = nullptr;
+  float* fx_out = nullptr;
   // fused decode scratch
   void* f_logits = nullptr;  // fused decode: tagged logits
   size_t f_logits_bytes = 0;
@@ -216,6 +223,8 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
   __half* xp = static_cast<__half*>(take(rows * D * 2));
   __half* part = static_cast<__half*>(take(rows * D * 2));
   float* dense_y = static_cast<float*>(take(c.dense ? T * D * 4 : 0));
+  uint16_t* fx_in = static_cast<uint16_t*>(take(c.fusion ? 3 * T * D * 2 : 0));
+  float* fx_out = static_cast<float*>(take(c.fusion ? 2 * T * D * 4 : 0));
   // fused decode (T <= 4)
   const size_t Tf = std::min<size_t>(T, 4);
   const size_t rows_f = Tf * K + Tf;
@@ -245,6 +254,8 @@ size_t carve(tsg_ctx ctx, const Caps& c, uint8_t* base) {
     ctx->xp = xp;
     ctx->partials = part;
     ctx->dense_y = c.dense ? dense_y : nullptr;
+    ctx->fx_in = c.fusion ? fx_in : nullptr;
+    ctx->fx_out = c.fusion ? fx_out : nullptr;
   }
   return align_up(off, 256);
 }
@@ -1334,6 +1345,87 @@ tsg_status tsg_moe_verify_rows_forward(tsg_ctx ctx, tsg_moe_layer L, const void*
     if (st != TSG_OK) return st;
   }
   if (ctx->profiling && ctx->prof_calls < ctx->prof_max) ++ctx->prof_calls;
+  return TSG_OK;
+}
+
+// Gemma's layer FFN between attention and the next layer: the fused setup
+// (post-attention norm, residual, the three normalised inputs), the dense
+// branch, the routed experts (routed on router_x, run on routed_x), and the
+// fused tail (the three post-norms, the residual, the layer scalar).
+tsg_status tsg_gemma_ffn_forward(tsg_ctx ctx, tsg_moe_layer L, const tsg_gemma_norms* norms,
+                                 void* hidden, uint32_t hidden_stride, const void* attn,
+                                 uint32_t attn_stride, uint32_t T) {
+  tsg_status st = check_common(ctx, L, hidden, hidden_stride, T, hidden, hidden_stride,
+                               TSG_DTYPE_BF16);
+  if (st != TSG_OK || T == 0) return st;
+  if (!norms || !norms->post_attn || !norms->pre_ffn || !norms->pre_ffn2 || !norms->post_dense ||
+      !norms->post_routed || !norms->post_ffn || !attn)
+    return fail(ctx, TSG_ERR_INVALID_ARG, "null norm weight or attention input");
+  if (attn_stride < L->desc.d || attn_stride % 8 || (reinterpret_cast<uintptr_t>(attn) & 15u))
+    return fail(ctx, TSG_ERR_INVALID_ARG, "attention stride is too small or not aligned");
+  if (L->desc.router_norm)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE,
+                "the fused Gemma path normalises its inputs itself: create the layer with router_norm = 0");
+  if (L->has_shared)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE,
+                "the fused Gemma path takes a dense branch (shared_f != f), not a shared expert slot");
+  if (L->desc.d > 4096) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "D above 4096");
+  Caps want = layer_caps(L, T);
+  want.fusion = 1;
+  st = ensure_workspace(ctx, want);
+  if (st != TSG_OK) return st;
+  st = take_pending_error(ctx);
+  if (st != TSG_OK) return st;
+  const uint32_t D = L->desc.d;
+  const size_t TD = static_cast<size_t>(T) * D;
+  uint16_t* router_x = ctx->fx_in;
+  uint16_t* routed_x = ctx->fx_in + TD;
+  uint16_t* dense_x = ctx->fx_in + 2 * TD;
+  float* h2 = ctx->fx_out;
+  float* h1 = ctx->fx_out + TD;
+  GemmaNorms n{};
+  n.post_attn = norms->post_attn;
+  n.pre_ffn = norms->pre_ffn;
+  n.pre_ffn2 = norms->pre_ffn2;
+  n.post_dense = norms->post_dense;
+  n.post_routed = norms->post_routed;
+  n.post_ffn = norms->post_ffn;
+  n.eps = norms->eps;
+  n.layer_scalar = norms->layer_scalar;
+  TSG_CUDA_TRY(ctx,
+               launch_gemma_setup(static_cast<uint16_t*>(hidden), hidden_stride,
+                                  static_cast<const uint16_t*>(attn), attn_stride,
+                                  static_cast<int>(T), static_cast<int>(D), n, router_x, routed_x,
+                                  dense_x, ctx->stream),
+               "gemma setup");
+  if (L->dense) {
+    st = run_dense_branch(ctx, L, dense_x, D, T, nullptr, h1, D, TSG_DTYPE_F32);
+    if (st != TSG_OK) return st;
+  }
+  // the routed experts: the router on router_x, the experts on routed_x
+  const RouterParams p = router_params(L, router_x, D, T);
+  ctx->last_T = T;
+  ctx->last_K = L->desc.top_k;
+  if (T <= ctx->decode_max_tokens) {
+    TSG_CUDA_TRY(ctx, launch_router_decode(p, ctx->rb, ctx->stream), "router (decode)");
+    if (fused_ok(ctx, L, T)) {
+      st = run_decode_fused(ctx, L, routed_x, D, T, ctx->rb.ids, ctx->rb.weights, nullptr, h2, D,
+                            TSG_DTYPE_F32, nullptr, nullptr, nullptr);
+    } else {
+      const RouterParams pr = router_params(L, routed_x, D, T);
+      TSG_CUDA_TRY(ctx, launch_rowprep(pr, ctx->rb, 1, ctx->stream), "row prep");
+      st = run_decode_experts(ctx, L, routed_x, D, T, nullptr, h2, D, TSG_DTYPE_F32);
+    }
+  } else {
+    TSG_CUDA_TRY(ctx, launch_router_prefill(p, ctx->rb, ctx->stream), "router (prefill)");
+    st = run_prefill_experts(ctx, L, routed_x, D, T, nullptr, h2, D, TSG_DTYPE_F32, true);
+  }
+  if (st != TSG_OK) return st;
+  TSG_CUDA_TRY(ctx,
+               launch_gemma_tail(h2, L->dense ? h1 : nullptr, static_cast<uint16_t*>(hidden),
+                                 hidden_stride, static_cast<int>(T), static_cast<int>(D), n,
+                                 ctx->stream),
+               "gemma tail");
   return TSG_OK;
 }
 

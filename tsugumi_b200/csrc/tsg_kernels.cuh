@@ -245,6 +245,24 @@ cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_reduce_token_major(const __half* partials, const float* w, int T, int K, int D,
                                       void* h2, int h2_f32, cudaStream_t s);
 
+// fusions.cu: the norms and residuals around Gemma's MoE block
+struct GemmaNorms {
+  const uint16_t* post_attn;    // [D] bf16: post-attention norm weight
+  const uint16_t* pre_ffn;      // [D] bf16: the dense branch's input norm weight
+  const uint16_t* pre_ffn2;     // [D] bf16: the routed experts' input norm weight
+  const uint16_t* post_dense;   // [D] bf16: the dense branch's output norm weight
+  const uint16_t* post_routed;  // [D] bf16: the routed output's norm weight
+  const uint16_t* post_ffn;     // [D] bf16: the summed branches' norm weight
+  float eps;
+  float layer_scalar;
+};
+cudaError_t launch_gemma_setup(uint16_t* hidden, uint32_t h_stride, const uint16_t* attn,
+                               uint32_t a_stride, int T, int D, const GemmaNorms& n,
+                               uint16_t* router_x, uint16_t* routed_x, uint16_t* dense_x,
+                               cudaStream_t s);
+cudaError_t launch_gemma_tail(const float* h2, const float* h1, uint16_t* hidden, uint32_t h_stride,
+                              int T, int D, const GemmaNorms& n, cudaStream_t s);
+
 // import.cu: one int4 matrix of a .moepack blob (U32 codes, BF16 scales of
 // `group` elements, optional BF16 biases) into codes bytes + fp16 32-group
 // scales, exactly (failures recorded in err: code 10 scale, 11 bias)

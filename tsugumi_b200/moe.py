@@ -139,6 +139,23 @@ class MoELayer:
               self.ctx.h)
         return y
 
+    def gemma_ffn(self, hidden, attn, norms: dict, eps: float = 1e-6,
+                  layer_scalar: float = 1.0):
+        """tsg_gemma_ffn_forward: Gemma's layer FFN with the adjacent norms
+        fused (fused_post_attn_setup / fused_layer_tail, fused.metal:190-374);
+        `hidden` (bf16 [T, D]) is updated in place.  `norms` holds bf16 [D]
+        tensors post_attn, pre_ffn, pre_ffn2, post_dense, post_routed,
+        post_ffn.  The layer is created with router_norm=False."""
+        keys = ("post_attn", "pre_ffn", "pre_ffn2", "post_dense", "post_routed", "post_ffn")
+        w = {k: norms[k].to(torch.bfloat16).contiguous() for k in keys}
+        n = _abi.GemmaNorms(*[_ptr(w[k]) for k in keys], float(eps), float(layer_scalar))
+        check(self.ctx.lib.tsg_gemma_ffn_forward(self.ctx.h, self.h, C.byref(n), _ptr(hidden),
+                                                 hidden.stride(0), _ptr(attn), attn.stride(0),
+                                                 hidden.shape[0]),
+              self.ctx.h)
+        self._gemma_norms = w  # alive until the stream has used them
+        return hidden
+
     def verify_rows(self, hidden, y=None, residual=None, out_dtype=None):
         """tsg_moe_verify_rows_forward: a speculative-verify block, each row
         bit-equal to forward() on that row alone (PrefillGroupedRoutedMoE
