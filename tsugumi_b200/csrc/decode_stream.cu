@@ -76,7 +76,6 @@ constexpr float kTwo20 = 1048576.0f;
 // unit order; the same split in every regime (T = 1 waves, rows owned), so
 // that one token's down rows come out of the same arithmetic either way.
 constexpr int kParts = 4;
-constexpr int kWavePairs = 4;  // waves: K pairs of one down unit, at most
 
 // Cross-CTA signalling (same scheme as the earlier fused decode kernel):
 // per-CTA launch epochs, the grid counter of each launch parity.
@@ -481,7 +480,7 @@ TSG_DEV void tma_load_4d_bar(uint32_t dst, const CUtensorMap* map, uint64_t* bar
 // 32 lanes, converged).  The slot's barrier expects one arrival per phase,
 // lane 0's expect-tx.  A down stage's scales are not copied: the warps that
 // compute its blocks load them directly.
-TSG_DEV void issue_stage(const StreamParams& p, const Plan& L, const Stage& sg, const int* slot_expert,
+__device__ __noinline__ void issue_stage(const StreamParams& p, const Plan& L, const Stage& sg, const int* slot_expert,
                          uint8_t* dst, uint64_t* bar, int lane) {
   const int D = p.D, F = p.F;
   const int slot = sg.kind_slot & 0xFF;
@@ -558,9 +557,9 @@ TSG_DEV float group_act_sum(const uint4* fr) {
 }
 
 // ---------------------------------------------------------------------------
-// waves (one router-routed token): the CTA's rows of y and the slot act
-// loads, kept out of line (each runs a few times per launch; the gate/up
-// loop keeps the instruction cache)
+// waves (one router-routed token): the down units of the CTA's rows of y,
+// kept out of line (each runs a few times per launch; the gate/up loop keeps
+// the instruction cache)
 // ---------------------------------------------------------------------------
 struct WaveRows {
   const uint8_t* down;  // [slots][drb]: the rows' down codes, then their scales
@@ -569,58 +568,39 @@ struct WaveRows {
   int F, K, nr;         // nr rows (in at most two 16-row tiles)
 };
 
-// One down unit of slot j -- 16-row tile t, pairs [p0, p0 + np) of K -- from
-// the slot's act words: word `lane` of pair p0 + i in v_i.  A pair's 32 words
-// are its eight operand chunks (two groups of 32 acts); the accumulator start
-// of a group is -8 * 2^-20 times the sum of its acts, summed across the
-// lanes that hold them.
-__device__ __noinline__ void wave_unit(const WaveRows& w, int j, int t, int kp, int p0, int np,
-                                       unsigned long long v0, unsigned long long v1,
-                                       unsigned long long v2, unsigned long long v3, int lane) {
-  const int F = w.F, GF = F / 32;
+// One down unit of slot j -- 16-row tile t, quarter kp of K -- from the
+// slot's acts in shared memory (act: [slots][F / 8] operand chunks, ast:
+// [slots][F / 32] accumulator starts), the arithmetic of the rows-owned
+// regime for one token.
+__device__ __noinline__ void wave_unit(const WaveRows& w, int j, int t, int kp, const uint4* act,
+                                       const float* ast, int lane) {
+  const int F = w.F, GF = F / 32, NP2 = F / 64;
   const int g = lane >> 2, c = lane & 3, m = lane >> 3, r8 = lane & 7;
+  const int p0 = (kp * NP2) / kParts, p1 = ((kp + 1) * NP2) / kParts;
   const uint8_t* dj = w.down + static_cast<uint32_t>(j) * w.drb;
   const __half* scs =
       reinterpret_cast<const __half*>(dj + static_cast<uint32_t>(w.nr) * (F / 2)) + 16 * t * GF;
   const uint32_t rowaddr = smem_u32(dj) + static_cast<uint32_t>(16 * t + r8 + 8 * (m & 1)) * (F / 2) +
                            static_cast<uint32_t>(m >> 1) * 16u;
-  // words 0, 1 of a chunk hold 16x values
-  const float wscale = c < 2 ? 0.0625f : 1.0f;
-  const unsigned long long wv[kWavePairs] = {v0, v1, v2, v3};
+  const uint4* af = act + static_cast<size_t>(j) * (F / 8) + c;
+  const float* as = ast + static_cast<size_t>(j) * GF;
   float acc0 = 0.0f, acc2 = 0.0f;
-#pragma unroll
-  for (int i = 0; i < kWavePairs; ++i) {
-    if (i < np) {
-      const int pr = p0 + i;
-      const uint32_t word = static_cast<uint32_t>(wv[i]);
-      const float2 h = h2_to_f2(word);
-      float gs = (h.x + h.y) * wscale;
-      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 1);
-      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 2);
-      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 4);
-      gs += __shfl_xor_sync(0xFFFFFFFFu, gs, 8);
-      const float c00 = -8.0f / kTwo20 * __shfl_sync(0xFFFFFFFFu, gs, 0);
-      const float c10 = -8.0f / kTwo20 * __shfl_sync(0xFFFFFFFFu, gs, 16);
-      uint4 b0, b1;
-      b0.x = __shfl_sync(0xFFFFFFFFu, word, 4 * c);
-      b0.y = __shfl_sync(0xFFFFFFFFu, word, 4 * c + 1);
-      b0.z = __shfl_sync(0xFFFFFFFFu, word, 4 * c + 2);
-      b0.w = __shfl_sync(0xFFFFFFFFu, word, 4 * c + 3);
-      b1.x = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c);
-      b1.y = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c + 1);
-      b1.z = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c + 2);
-      b1.w = __shfl_sync(0xFFFFFFFFu, word, 16 + 4 * c + 3);
-      if (g != 0) b0 = b1 = make_uint4(0u, 0u, 0u, 0u);  // one token: column 0
-      uint32_t q0, q1, q2, q3;
-      ldsm_x4(rowaddr + static_cast<uint32_t>(pr) * 32u, q0, q1, q2, q3);
-      float d0[4], d1[4];
-      mma_group(d0, q0, q1, b0, c == 0 ? c00 : 0.0f, 0.0f);
-      mma_group(d1, q2, q3, b1, c == 0 ? c10 : 0.0f, 0.0f);
-      const float2 sr = h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + g * GF + 2 * pr));
-      const float2 sh = h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + (g + 8) * GF + 2 * pr));
-      acc0 = fmaf(sr.y, d1[0], fmaf(sr.x, d0[0], acc0));
-      acc2 = fmaf(sh.y, d1[2], fmaf(sh.x, d0[2], acc2));
-    }
+  // (unrolled: the pairs' MMAs overlap; the sums stay in pair order)
+#pragma unroll 4
+  for (int pr = p0; pr < p1; ++pr) {
+    uint32_t q0, q1, q2, q3;
+    ldsm_x4(rowaddr + static_cast<uint32_t>(pr) * 32u, q0, q1, q2, q3);
+    const uint4 b0 = g == 0 ? af[8 * pr] : make_uint4(0u, 0u, 0u, 0u);  // one token: column 0
+    const uint4 b1 = g == 0 ? af[8 * pr + 4] : make_uint4(0u, 0u, 0u, 0u);
+    const float c00 = c == 0 ? as[2 * pr] : 0.0f;
+    const float c10 = c == 0 ? as[2 * pr + 1] : 0.0f;
+    float d0[4], d1[4];
+    mma_group(d0, q0, q1, b0, c00, 0.0f);
+    mma_group(d1, q2, q3, b1, c10, 0.0f);
+    const float2 sr = h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + g * GF + 2 * pr));
+    const float2 sh = h2_to_f2(*reinterpret_cast<const uint32_t*>(scs + (g + 8) * GF + 2 * pr));
+    acc0 = fmaf(sr.y, d1[0], fmaf(sr.x, d0[0], acc0));
+    acc2 = fmaf(sh.y, d1[2], fmaf(sh.x, d0[2], acc2));
   }
   if (c == 0) {
     float* o = w.sv + (static_cast<size_t>(kp) * (w.K + 1) + j) * 32 + 16 * t;
@@ -642,6 +622,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t bar_act, bar_act2;  // compute warps, once per launch
   __shared__ __align__(8) uint64_t bar_go;              // warp 0: every CTA's acts are out
   __shared__ __align__(8) uint64_t bar_down;             // waves: the CTA's down rows have landed
+  __shared__ __align__(8) uint64_t bar_ld[kMaxSlots];    // waves: a slot's act words have landed
+  __shared__ __align__(8) uint64_t bar_slot[kMaxSlots];  // waves: a slot's acts are unpacked
   __shared__ int s_issued[kMaxRing];
   __shared__ Stage s_stage[kMaxStages];
   __shared__ int s_ids[kMaxTok][kMaxK];
@@ -693,6 +675,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     s_issued[tid - 32] = 0;
   }
   if (tid == 64) s_epoch = __ldcg(&sig->epoch[bid]) + 1u;  // this launch's tag
+  if (tid >= 128 && tid < 128 + kMaxSlots) {
+    mbar_init(&bar_ld[tid - 128], 1);
+    mbar_init(&bar_slot[tid - 128], 1);
+    fence_mbar_init();
+  }
   if (tid == 96) {
     mbar_init(&bar_down, 1);
     mbar_init(&bar_act, kWarps);
@@ -1115,11 +1102,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m = lane >> 3, r8 = lane & 7;
   bool failed = false;
   // ---- waves (T = 1): the CTA's rows of y, slot by slot ----
-  // A compute warp has at most one down unit per slot (unit u of slot j goes
-  // to warp (j U + u) mod 15) and pulls the act words the unit needs into
-  // registers: requested once the slot's last wave is due (after this CTA's
-  // own stage of it), checked after each later gate/up stage, the words not
-  // out yet requested again.  No act passes through shared memory.
+  // Once its gate/up stages are done, the reduction warp bulk-loads every
+  // slot's tagged act words into the (then free) ring, checks the tags
+  // (loading again a slot with a word not out yet), unpacks the acts and
+  // their accumulator starts next to them and releases the slot; a compute
+  // warp has at most one down unit per slot (unit u of slot j goes to warp
+  // (j U + u) mod 15) and runs it from shared memory once the slot is in.
   const int wr0 = 4 * ((bid * (D / 4)) / G);
   const int wnr = 4 * (((bid + 1) * (D / 4)) / G) - wr0;
   const int wU = ((wnr + 15) / 16) * kParts;
@@ -1133,51 +1121,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   wrow.F = F;
   wrow.K = K;
   wrow.nr = wnr;
-  bool down_in = false;  // the down region has landed
-  bool wpend = false;    // the act words of slot wj's unit are requested
-  unsigned long long wv0 = 0, wv1 = 0, wv2 = 0, wv3 = 0;
-  int wt = 0, wkp = 0, wp0 = 0, wnp = 0;
-  auto wave_seek = [&](int j) {  // the first slot >= j with a unit of this warp
-    for (; j < nslots; ++j)
-      if (((warp - j * wU) % kWarps + kWarps) % kWarps < wU) break;
-    return j;
-  };
-  int wj = waves ? wave_seek(0) : nslots;
-  auto slot_wave = [&](int j) { return ((j + 1) * F8 - 1) / G; };
-  auto wave_load = [&](bool all) {
-    const unsigned long long* src = p.hact + static_cast<size_t>(wj) * (F / 2) + 32 * wp0 + lane;
-    if (0 < wnp && (all || static_cast<uint32_t>(wv0 >> 32) != tag)) wv0 = ld_relaxed_u64(src);
-    if (1 < wnp && (all || static_cast<uint32_t>(wv1 >> 32) != tag)) wv1 = ld_relaxed_u64(src + 32);
-    if (2 < wnp && (all || static_cast<uint32_t>(wv2 >> 32) != tag)) wv2 = ld_relaxed_u64(src + 64);
-    if (3 < wnp && (all || static_cast<uint32_t>(wv3 >> 32) != tag)) wv3 = ld_relaxed_u64(src + 96);
-  };
-  auto wave_in = [&]() {  // every word of the unit carries this launch's tag
-    const bool ok = (wnp <= 0 || static_cast<uint32_t>(wv0 >> 32) == tag) &&
-                    (wnp <= 1 || static_cast<uint32_t>(wv1 >> 32) == tag) &&
-                    (wnp <= 2 || static_cast<uint32_t>(wv2 >> 32) == tag) &&
-                    (wnp <= 3 || static_cast<uint32_t>(wv3 >> 32) == tag);
-    return __all_sync(0xFFFFFFFFu, ok);
-  };
-  auto wave_start = [&]() {  // the unit of slot wj, and its act words requested
-    const int u = ((warp - wj * wU) % kWarps + kWarps) % kWarps;
-    const int NP2 = F / 64;
-    wt = u / kParts;
-    wkp = u - wt * kParts;
-    wp0 = (wkp * NP2) / kParts;
-    wnp = ((wkp + 1) * NP2) / kParts - wp0;
-    wave_load(true);
-    wpend = true;
-  };
-  auto wave_run = [&]() -> bool {  // the unit (once the down rows are in); then the next slot
-    if (!down_in) {
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait_inl(&bar_down, 0, err))) return false;
-      down_in = true;
-    }
-    wave_unit(wrow, wj, wt, wkp, wp0, wnp, wv0, wv1, wv2, wv3, lane);
-    wpend = false;
-    wj = wave_seek(wj + 1);
-    return true;
-  };
+  // the ring after the gate/up stages: [slots][F / 2] tagged words, then the
+  // acts [slots][F / 8] uint4, then their accumulator starts [slots][F / 32]
+  const uint32_t wstg_bytes = static_cast<uint32_t>(K + 1) * static_cast<uint32_t>(F) * 4u;
+  unsigned long long* wstg = reinterpret_cast<unsigned long long*>(ring);
+  uint4* wact = reinterpret_cast<uint4*>(ring + wstg_bytes);
+  float* wast = reinterpret_cast<float*>(ring + wstg_bytes + static_cast<uint32_t>(K + 1) * F * 2u);
   const int GF = F / 32;
   uint4* afr = reinterpret_cast<uint4*>(smem + L.act_off);
   float* ast = reinterpret_cast<float*>(smem + L.ast_off);
@@ -1244,7 +1193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c < 2)
           *reinterpret_cast<float4*>(mine + 4 * (2 * g + c)) = make_float4(acc[0], acc[1], acc[2], acc[3]);
       }
-    } else if (rows_owned(T)) {
+    } else if (!waves && rows_owned(T)) {
       // ---- (reached once, at the first down stage) ----
       // every slot's acts into shared memory: warp 0 first waits until every
       // CTA has flagged its gate/up blocks published, so that the tagged
@@ -1512,43 +1461,76 @@ __global__ void __launch_bounds__(kThreads, 1)
     // release the stage to the reduction warp (which refills its ring slot)
     __syncwarp();
     if (lane == 0) mbar_arrive(&bar_rel[rs]);
-    if (waves)  // between stages: the down units whose acts are in
-      while (wj < nslots) {
-        if (!wpend) {
-          if (s >= slot_wave(wj)) wave_start();  // checked after the next stage
-          break;
-        }
-        if (!wave_in()) {
-          wave_load(false);
-          break;
-        }
-        if (!wave_run()) {
-          failed = true;
-          break;
-        }
-      }
   }
   if (waves && !failed) {
-    // the remaining units: one round trip per check
-    const unsigned long long t0 = global_timer_ns();
-    uint32_t spin = 0;
-    while (wj < nslots) {
-      if (!wpend) wave_start();
-      if (!wave_in()) {
-        if ((++spin & 15u) == 0u &&
-            __any_sync(0xFFFFFFFFu, lane == 0 && poll_give_up(t0, err))) {
+    // 1. the slots this warp brings in (j = warp, warp + 15, ...): once the
+    // reduction warp's copy of a slot's tagged act words has landed, every
+    // word must carry this launch's tag (else the slot is copied again);
+    // then its acts and accumulator starts (in the order the rows-owned
+    // regime sums them) are unpacked next to the words and the slot is
+    // released
+    const uint32_t sbytes = static_cast<uint32_t>(F) * 4u;  // F / 2 words
+    for (int j = warp; j < nslots && !failed; j += kWarps) {
+      uint32_t par = 0;
+      const unsigned long long t0 = global_timer_ns();
+      for (;;) {
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait_inl(&bar_ld[j], par, err))) {
           failed = true;
           break;
         }
-        // (every CTA's waiting warps poll the same few lines: space the polls)
-        __nanosleep(256);
-        wave_load(false);
-        continue;
+        par ^= 1u;
+        if (lane == 0 && p.stamps && j < 8) stamp_at(p.stamps, bid * kStamps + 48 + j);  // debug
+        const unsigned long long* wv = wstg + static_cast<size_t>(j) * (F / 2);
+        bool ok = true;
+        for (int w = lane; w < F / 2; w += 32) ok &= static_cast<uint32_t>(wv[w] >> 32) == tag;
+        if (__all_sync(0xFFFFFFFFu, ok)) break;
+        if (__any_sync(0xFFFFFFFFu, lane == 0 && poll_give_up(t0, err))) {
+          failed = true;
+          break;
+        }
+        fence_async_shared();  // (this warp's reads of the copy come first)
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_ld[j], sbytes);
+          bulk_load(wstg + static_cast<size_t>(j) * (F / 2), p.hact + static_cast<size_t>(j) * (F / 2),
+                    sbytes, &bar_ld[j]);
+        }
       }
-      if (!wave_run()) {
+      if (failed) {
+        if (lane == 0) drain_wait(&bar_ld[j], par);  // a copy still in flight lands first
+        break;
+      }
+      const unsigned long long* wv = wstg + static_cast<size_t>(j) * (F / 2);
+      uint32_t* a32 = reinterpret_cast<uint32_t*>(wact + static_cast<size_t>(j) * F8);
+      for (int w = lane; w < F / 2; w += 32) a32[w] = static_cast<uint32_t>(wv[w]);
+      __syncwarp();
+      for (int grp = lane; grp < F / 32; grp += 32)
+        wast[static_cast<size_t>(j) * (F / 32) + grp] =
+            -8.0f / kTwo20 * group_act_sum(wact + static_cast<size_t>(j) * F8 + 4 * grp);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar_slot[j]);
+        if (p.stamps && j < 8) stamp_at(p.stamps, bid * kStamps + 32 + j);  // debug: slot in
+      }
+    }
+    // 2. this warp's down units, slot by slot, as the slots come in
+    // (the waits suspend in hardware: a spinning warp would take issue
+    // slots from the reduction warp that brings the slots in)
+    stamp(41);  // debug: warp 0's slots brought in
+    if (!__all_sync(0xFFFFFFFFu, mbar_sleep(&bar_down, 0, err))) failed = true;
+    stamp(42);  // debug: warp 0 sees the down rows
+    int dbg_k = 0;
+    for (int j = 0; j < nslots && !failed; ++j) {
+      const int u = ((warp - j * wU) % kWarps + kWarps) % kWarps;
+      if (u >= wU) continue;
+      if (!__all_sync(0xFFFFFFFFu, mbar_sleep(&bar_slot[j], 0, err))) {
         failed = true;
         break;
       }
+      if (dbg_k < 6) stamp(56 + 2 * dbg_k);  // debug: warp 0's unit k starts
+      wave_unit(wrow, j, u / kParts, u % kParts, wact, wast, lane);
+      if (dbg_k < 6) stamp(57 + 2 * dbg_k);  // debug: and ends
+      ++dbg_k;
     }
     stamp(23);  // debug: warp 0's down units done
   }
@@ -1653,6 +1635,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (s + NS < nst) {
         issue_stage(p, L, s_stage[s + NS], s_slot_expert, base, &bar_st[rs], lane);
         if (lane == 0) ++s_issued[rs];
+      }
+    }
+    if (waves && !failed && lane == 0) {
+      // every stage is released, so the ring is free: each slot's tagged act
+      // words in one bulk copy, all requested at once (the compute warps
+      // check, unpack and release them)
+      if (p.stamps) stamp_at(p.stamps, bid * kStamps + 40);  // debug: loads start
+      const uint32_t sbytes = static_cast<uint32_t>(F) * 4u;  // F / 2 words
+      for (int j = 0; j < nslots; ++j) {
+        mbar_arrive_expect_tx(&bar_ld[j], sbytes);
+        bulk_load(wstg + static_cast<size_t>(j) * (F / 2), p.hact + static_cast<size_t>(j) * (F / 2),
+                  sbytes, &bar_ld[j]);
       }
     }
   }
@@ -1840,19 +1834,22 @@ int ring_slots_for(int T, int D, int F, int K, int G, bool waves = false) {
   return 0;
 }
 
-// Whether one router-routed token can run in waves: a down unit's pairs at
-// most kWavePairs (one act word per lane each), a CTA's rows of y in two
+// Whether one router-routed token can run in waves: a CTA's rows of y in two
 // 16-row tiles, the whole plan in shared memory with room for the router
-// rows and order keys.
+// rows and order keys, and the slots' acts in the ring after the stages.
 bool waves_ok(int D, int F, int K, int E, int G) {
-  if (F / 64 > kParts * kWavePairs || F / 64 < kParts) return false;
+  if (F / 64 < kParts) return false;
   if (4 * ((D / 4 + G - 1) / G) > 32) return false;
   if ((static_cast<long long>(K + 1) * (F / 8) + G - 1) / G > kMaxStages) return false;
   const int ns = ring_slots_for(1, D, F, K, G, true);
   if (ns < 2) return false;
   const Plan L = make_plan(1, D, F, K, G, ns, true);
+  // after the stages the ring holds every slot's act words, acts and
+  // accumulator starts
+  const uint64_t acts = static_cast<uint64_t>(K + 1) * (static_cast<uint64_t>(F) * 6u + (F / 32) * 4u);
   return 2u * static_cast<uint32_t>(D) * 4u + static_cast<uint32_t>(E) * 4u <=
-         static_cast<uint32_t>(ns) * L.sb;
+             static_cast<uint32_t>(ns) * L.sb &&
+         acts <= static_cast<uint64_t>(ns) * L.sb;
 }
 
 // An upper bound of the stages of one CTA's share (largest slot count).
