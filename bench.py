@@ -517,21 +517,35 @@ def run_ep_sweep(device, args, rank, world, local):
                 lay.forward(x, y=y)
         torch.cuda.synchronize()
         steps = 3
-        if world > 1:
-            dist.barrier(device_ids=[local])
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
+
+        def timed() -> float:
+            if world > 1:
+                dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                for lay in lays:
+                    lay.forward(x, y=y)
+            e1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / (steps * len(lays))], device=device)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        nccl_ms = None
+        if group is not None:
+            # the NCCL all-to-all transport first, for comparison; then the
+            # default peer-memory transport, which the entry reports
+            ctx.set_option("ep_transport", 0)
             for lay in lays:
                 lay.forward(x, y=y)
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / (steps * len(lays))
-        t = torch.tensor([ms], device=device)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+            nccl_ms = timed()
+            ctx.set_option("ep_transport", 1)
+            for lay in lays:
+                lay.forward(x, y=y)
+        ms = timed()
         f = tensors[0]["f"]
         k = tensors[0]["top_k"]
         flops = 2.0 * total * k * 3 * d * f
@@ -539,12 +553,12 @@ def run_ep_sweep(device, args, rank, world, local):
             "world": world, "tokens": total, "tokens_per_rank": T,
             "ms_per_layer": ms, "layer_tokens_per_s": total / (ms / 1e3),
             "routed_tflops": flops / (ms / 1e3) / 1e12,
-            "path": "expert parallel (NCCL all-to-all)" if group is not None
+            "path": "expert parallel (rows and outputs through peer memory)" if group is not None
                     else "single GPU prefill"}
         if group is not None:
+            entry["nccl_transport_ms_per_layer"] = nccl_ms
+            entry["phase_ms"] = lays[0].phase_ms()  # the last timed call (second layer)
             entry.update(ep_check_bit_equal(ctx, tensors, lays, x, world, local))
-            if getattr(lays[0], "phase_ms", None) is not None:
-                entry["phase_ms"] = lays[0].phase_ms()
         out[f"ep_prefill_{name}"] = entry
         for lay in lays:
             lay.close()

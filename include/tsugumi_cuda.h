@@ -139,7 +139,9 @@ TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
  * as batched GEMVs; default 16, 0 for the tensor-core contraction only) and
  * "debug_phase_stamps" (a device address of
  * num_sms x 8 uint64 the fused decode kernel fills with %globaltimer stamps
- * at its phase boundaries, or 0 for none). */
+ * at its phase boundaries, or 0 for none), "ep_transport" (expert
+ * parallelism: 1, the default, moves rows through peer memory; 0 through
+ * NCCL all-to-all; every rank of a group sets the same value). */
 TSG_API tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char *name, int64_t value);
 /* Pre-allocates the workspace for up to max_tokens tokens of this layer's
  * shape, so later calls allocate nothing (required before stream capture). */
@@ -366,12 +368,17 @@ TSG_API tsg_status tsg_last_routing(tsg_ctx ctx, const uint32_t **ids, const flo
  * sequence (RealForwardRunner.swift:1840-2640 prefill) is kept on each rank,
  * with the experts split contiguously over R ranks.  Per layer, each rank
  * routes its own tokens, exchanges per-expert pair counts, sends each
- * normalised fp16 token row to the rank that owns its expert (NCCL
- * all-to-all over NVLink), runs the grouped contraction on the rows it
- * received (plus the shared expert on its own tokens), returns the expert
- * outputs and combines its tokens in rank order -- the same arithmetic as one
- * GPU, so the outputs are bit-equal.  NCCL (libnccl.so.2) is loaded when
- * tsg_ep_init is first called. */
+ * normalised fp16 token row to the rank that owns its expert, runs the
+ * grouped contraction on the rows it received (plus the shared expert on its
+ * own tokens), returns the expert outputs and combines its tokens in rank
+ * order -- the same arithmetic as one GPU, so the outputs are bit-equal.
+ * With the peer transport (default, at most 16 ranks) a kernel stores each
+ * token row once per owner rank straight into the owners' buffers over
+ * NVLink (the owner expands them into pair rows), and the contraction's
+ * epilogue stores each output row into its token's rank's buffer (buffers
+ * mapped between the processes with CUDA IPC); NCCL carries the counts and
+ * the barriers.  With "ep_transport" 0 NCCL all-to-all carries the rows.
+ * NCCL (libnccl.so.2) is loaded when tsg_ep_init is first called. */
 #define TSG_EP_UNIQUE_ID_BYTES 128
 
 /* Writes a new NCCL unique id (TSG_EP_UNIQUE_ID_BYTES) on one rank; the
@@ -387,11 +394,21 @@ TSG_API tsg_status tsg_ep_init(tsg_ctx ctx, const void *unique_id, int rank, int
  * rank * E / world, and the blobs of the E / world local experts follow at
  * expert_stride.  E must be a multiple of world.  Every rank calls this
  * collectively, each with its own tokens (T may differ between ranks).
- * Synchronises the context's stream once (after the count exchange). */
+ * Synchronises the context's stream once (after the count exchange), and
+ * again when an exchange buffer grows. */
 TSG_API tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer layer, uint32_t expert_first,
                                             const void *hidden_bf16, uint32_t hidden_stride,
                                             uint32_t T, const float *residual_f32, void *y,
                                             uint32_t y_stride, tsg_dtype y_dtype);
+
+/* Device time, in ms, of the phases of this context's last peer-transport
+ * tsg_ep_moe_block_forward (waits for it): [0] routing and sorting, [1] the
+ * count exchange and the plan (host time included), [2] the row dispatch and
+ * its barrier, [3] the expansion of received token rows into pair rows,
+ * [4] the gate/up contraction, [5] the down contraction with the output
+ * stores, [6] the return barrier, [7] the combine.  Writes min(n, 8)
+ * values. */
+TSG_API tsg_status tsg_ep_phase_ms(tsg_ctx ctx, float *ms, int n);
 
 #ifdef __cplusplus
 }

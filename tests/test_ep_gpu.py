@@ -18,11 +18,13 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parent.parent
 WORLD = 2
 CASES = [
-    # config, tokens per rank, skew
+    # config, tokens of rank 0 (rank r has 3r more), skew
     ("tiny", 16, None),
     ("gemma", 700, 1.1),
     ("qwen", 300, None),
+    ("gemma_dense", 200, 1.1),
 ]
+TRANSPORTS = (1, 0)  # peer memory, NCCL all-to-all
 
 
 def _free_port() -> int:
@@ -51,23 +53,29 @@ def _rank_main(rank: int, port: int, q):
         ctx.set_option("gemv_max_tokens", 0)
         group = ep.ExpertParallelGroup.from_torch_distributed(ctx)
         msgs = []
-        for name, T, skew in CASES:
-            t = device_layer_tensors(name, 4242, skew, dev)
-            full = tb.MoELayer(ctx, t)
-            shard = ep.EPMoELayer(group, t)
-            g = torch.Generator(device=dev)
-            g.manual_seed(77)
-            x_all = torch.randn((WORLD * T, t["d"]), generator=g, device=dev).to(torch.bfloat16)
-            x = x_all[rank * T:(rank + 1) * T].contiguous()
-            want = full.forward(x, out_dtype=torch.float32)
-            got = shard.forward(x, out_dtype=torch.float32)
-            got2 = shard.forward(x, out_dtype=torch.float32)  # second call, warm buffers
-            ctx.sync()
-            same = torch.equal(got, want) and torch.equal(got2, want)
-            diff = float((got - want).abs().max())
-            msgs.append((name, same, diff))
-            shard.close()
-            full.close()
+        for transport in TRANSPORTS:
+            ctx.set_option("ep_transport", transport)
+            for name, T0, skew in CASES:
+                t = device_layer_tensors(name, 4242, skew, dev)
+                full = tb.MoELayer(ctx, t)
+                shard = ep.EPMoELayer(group, t)
+                g = torch.Generator(device=dev)
+                g.manual_seed(77)
+                Ts = [T0 + 3 * r for r in range(WORLD)]
+                x_all = torch.randn((sum(Ts), t["d"]), generator=g, device=dev).to(torch.bfloat16)
+                x = x_all[sum(Ts[:rank]):sum(Ts[:rank + 1])].contiguous()
+                want = full.forward(x, out_dtype=torch.float32)
+                got = shard.forward(x, out_dtype=torch.float32)
+                got2 = shard.forward(x, out_dtype=torch.float32)  # second call, warm buffers
+                ctx.sync()
+                same = torch.equal(got, want) and torch.equal(got2, want)
+                diff = float((got - want).abs().max())
+                msgs.append((f"{name} transport {transport}", same, diff))
+                if transport == 1:
+                    ph = shard.phase_ms()
+                    msgs.append((f"{name} phases", all(v >= 0 for v in ph.values()), 0.0))
+                shard.close()
+                full.close()
         dist.barrier()
         ctx.close()
         dist.destroy_process_group()

@@ -100,6 +100,7 @@ SIGNATURES = [
     ("tsg_ep_unique_id", _S, [_P]),
     ("tsg_ep_init", _S, [_P, _P, C.c_int, C.c_int]),
     ("tsg_ep_moe_block_forward", _S, [_P, _P, _U, _P, _U, _U, _P, _P, _U, C.c_int]),
+    ("tsg_ep_phase_ms", _S, [_P, _P, C.c_int]),
     ("tsg_plan_routed_gemm", _S, [_P, _U, _U, _U, _P, _U, C.POINTER(_U), _P, _P, _P, _U,
                                   C.POINTER(_U)]),
     ("tsg_moe_experts_decode", _S, [_P, _P, _P, _U, _U, _P, _P, _P, _P, _U, C.c_int]),

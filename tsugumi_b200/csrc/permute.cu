@@ -369,7 +369,146 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* x, uin
   }
 }
 
+// One CTA per owner rank, 1024 tokens per pass: a token is on owner o when
+// one of its experts is; its slot is the count of such tokens before it.
+__global__ void __launch_bounds__(1024) ep_owner_slots_kernel(const uint32_t* ids, int T, int K,
+                                                              int El, uint32_t* slots,
+                                                              uint32_t* counts) {
+  __shared__ uint32_t warp_sum[32];
+  __shared__ uint32_t carry;
+  const uint32_t o = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < T; base += 1024) {
+    const int t = base + static_cast<int>(threadIdx.x);
+    bool on = false;
+    if (t < T)
+      for (int k = 0; k < K; ++k) on |= ids[static_cast<size_t>(t) * K + k] / static_cast<uint32_t>(El) == o;
+    const uint32_t bal = __ballot_sync(0xffffffffu, on);
+    if (lane == 0) warp_sum[warp] = __popc(bal);
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t v = warp_sum[lane];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
+      }
+      warp_sum[lane] = v;  // inclusive
+    }
+    __syncthreads();
+    const uint32_t before = carry + (warp ? warp_sum[warp - 1] : 0u) + __popc(bal & ((1u << lane) - 1u));
+    if (t < T) slots[static_cast<size_t>(o) * T + t] = on ? before : kEpNoSlot;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += warp_sum[31];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) counts[o] = carry;
+}
+
+// Threads write the pairs' map entries (grid-stride); warps write the rows,
+// one per (owner, token).  Every index is checked against its buffer before
+// the store.
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant__ EpDispatch d) {
+  const uint32_t gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t nthr = gridDim.x * blockDim.x;
+  const uint32_t El = static_cast<uint32_t>(d.experts_per_rank);
+  const uint32_t R = static_cast<uint32_t>(d.world), T = static_cast<uint32_t>(d.T);
+  for (uint32_t i = gtid; i < static_cast<uint32_t>(d.P); i += nthr) {
+    const Pair pr = d.sorted_pairs[i];
+    const uint32_t o = pr.expert / El;
+    if (o >= R || pr.token >= T) {
+      flag_error(d.err, TSG_DEVERR_BOUNDS);
+      continue;
+    }
+    const uint32_t k = i - d.send_off[o];
+    const uint32_t slot = d.slots[static_cast<size_t>(o) * T + pr.token];
+    const uint32_t e = d.map0[o] + k;
+    if (i < d.send_off[o] || k >= d.send_cnt[o] || slot >= d.n_rows[o] || e >= d.map_cap[o]) {
+      flag_error(d.err, TSG_DEVERR_BOUNDS);
+      continue;
+    }
+    d.map[o][e] = d.row0[o] + slot;
+  }
+  const uint32_t w = gtid >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w < R * T) {
+    const uint32_t o = w / T, t = w % T;
+    const uint32_t slot = d.slots[static_cast<size_t>(o) * T + t];
+    if (slot != kEpNoSlot) {
+      const uint32_t row = d.row0[o] + slot;
+      if (slot >= d.n_rows[o] || row >= d.row_cap[o]) {
+        if (lane == 0) flag_error(d.err, TSG_DEVERR_BOUNDS);
+      } else {
+        const float inv = d.inv_rms[t];
+        const uint4* src = reinterpret_cast<const uint4*>(d.x + static_cast<size_t>(t) * d.x_stride);
+        uint4* dst = reinterpret_cast<uint4*>(d.rows[o] + static_cast<size_t>(row) * d.D);
+        for (int c = lane; c < d.D / 8; c += 32) {
+          const uint4 v = __ldg(src + c);
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+          uint32_t h4[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float a = __uint_as_float(wv[j] << 16);
+            const float b = __uint_as_float(wv[j] & 0xFFFF0000u);
+            __half2 h = __floats2half2_rn(a * inv, b * inv);
+            h4[j] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          dst[c] = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+        }
+      }
+    }
+  }
+  // the stores reach the owners before this thread's later writes (the
+  // owners read them after a collective that follows this kernel)
+  __threadfence_system();
+}
+
+__global__ void __launch_bounds__(256) ep_expand_kernel(const __half* rows, uint32_t rows_cap,
+                                                        const uint32_t* map, int n, int D,
+                                                        __half* xp, uint32_t* err) {
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const uint32_t r = map[i];
+  if (r >= rows_cap) {
+    if (lane == 0) flag_error(err, TSG_DEVERR_BOUNDS);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(rows + static_cast<size_t>(r) * D);
+  uint4* dst = reinterpret_cast<uint4*>(xp + static_cast<size_t>(i) * D);
+  for (int c = lane; c < D / 8; c += 32) dst[c] = src[c];
+}
+
 }  // namespace
+
+cudaError_t launch_ep_owner_slots(const uint32_t* ids, int T, int K, int experts_per_rank,
+                                  int world, uint32_t* slots, uint32_t* counts, cudaStream_t s) {
+  if (world < 1 || world > kEpMaxRanks || experts_per_rank < 1 || T < 0) return cudaErrorInvalidValue;
+  ep_owner_slots_kernel<<<world, 1024, 0, s>>>(ids, T, K, experts_per_rank, slots, counts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_dispatch(const EpDispatch& d, cudaStream_t s) {
+  if (d.P <= 0 || d.T <= 0) return cudaSuccess;
+  if (d.world < 1 || d.world > kEpMaxRanks || d.experts_per_rank < 1 || d.D % 8)
+    return cudaErrorInvalidValue;
+  const int warps_per_cta = 8;
+  const int warps = d.world * d.T;
+  ep_dispatch_kernel<<<(warps + warps_per_cta - 1) / warps_per_cta, 256, 0, s>>>(d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_expand(const __half* rows, uint32_t rows_cap, const uint32_t* map, int n,
+                             int D, __half* xp, uint32_t* err, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (D % 8) return cudaErrorInvalidValue;
+  const int warps_per_cta = 8;
+  ep_expand_kernel<<<(n + warps_per_cta - 1) / warps_per_cta, 256, 0, s>>>(rows, rows_cap, map, n,
+                                                                           D, xp, err);
+  return cudaGetLastError();
+}
 
 int permute_chunks(int P) { return (P + kChunk - 1) / kChunk; }
 

@@ -110,6 +110,31 @@ struct tsg_ctx_s {
   RowTile* ep_h_tiles = nullptr;       // pinned staging
   uint32_t* ep_ntiles = nullptr;       // device [1] (follows ep_tiles' capacity)
   size_t ep_tiles_cap = 0;
+  // peer-memory transport (ep_transport 1).  Buffers, by kind (EpBuf):
+  // the pair rows expanded for the contraction (then this rank's
+  // shared-expert rows) and their activations, local; and the three that
+  // peers write -- the returned outputs in this rank's sorted order (then its
+  // shared rows), the token rows received (one per token and owner) and the
+  // map from each received pair to its token row.  ep_caps holds every
+  // rank's capacities, the same on every rank (each is a function of the
+  // exchanged counts); ep_peer the views of the peers' buffers.
+  int ep_transport = 1;                // 0: NCCL all-to-all; 1: peer memory
+  void* ep_buf[5] = {};
+  size_t ep_buf_elems[5] = {};         // this rank's allocations
+  std::vector<size_t> ep_caps[6];      // [kind][world] elements; [5]: row tiles
+  std::vector<void*> ep_peer[5];       // [kind][world]; own entry = own buffer
+  uint32_t* ep_slots = nullptr;        // [world][T] token slots per owner
+  size_t ep_slots_cap = 0;
+  uint32_t* ep_ag = nullptr;           // device: send [kAgWords], receive [world][kAgWords], barriers
+  uint32_t* ep_h_ag = nullptr;         // pinned copy of the received words
+  RowTile* ep_ptiles = nullptr;        // device row tiles, then their count
+  RowTile* ep_h_ptiles = nullptr;      // pinned staging
+  uint32_t* ep_pntiles = nullptr;      // device [1] (follows ep_ptiles' capacity)
+  size_t ep_ptiles_cap = 0;
+  unsigned long long* ep_tile_out = nullptr;    // device [ep_ptiles_cap]: per tile, rows' destination
+  unsigned long long* ep_h_tile_out = nullptr;  // pinned staging
+  cudaEvent_t ep_ev[9] = {};           // phase boundaries of the last call (peer transport)
+  bool ep_ev_ok = false;
 };
 
 struct tsg_moe_layer_s {
@@ -621,6 +646,8 @@ struct NcclApi {
   ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*group_start)() = nullptr;
   ncclResult_t (*group_end)() = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -641,8 +668,9 @@ const NcclApi& nccl() {
     api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
     api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.send && api.recv &&
-             api.group_start && api.group_end && api.error_string;
+             api.group_start && api.group_end && api.error_string && api.all_gather;
   });
   return api;
 }
@@ -659,9 +687,58 @@ tsg_status nccl_fail(tsg_ctx ctx, ncclResult_t r, const char* where) {
     if (r__ != ncclSuccess) return nccl_fail(ctx, r__, where);      \
   } while (0)
 
+enum EpBuf { kEpXp = 0, kEpAct, kEpRet, kEpRows, kEpMap, kEpBufs };
+constexpr size_t kEpElemBytes[kEpBufs] = {2, 2, 2, 2, 4};
+constexpr bool kEpShared[kEpBufs] = {false, false, true, true, true};  // written by peers
+
+// Unmaps the peers' buffers (the peers keep their own) and forgets every
+// rank's capacities, so the next call grows them all again.
+void close_peer_views(tsg_ctx ctx) {
+  for (int b = 0; b < kEpBufs; ++b) {
+    std::vector<void*>& v = ctx->ep_peer[b];
+    for (size_t q = 0; q < v.size(); ++q)
+      if (static_cast<int>(q) != ctx->ep_rank && v[q] && kEpShared[b]) cudaIpcCloseMemHandle(v[q]);
+    v.assign(v.size(), nullptr);
+  }
+  for (std::vector<size_t>& c : ctx->ep_caps) c.assign(c.size(), 0);
+}
+
+// Word layout of ep_ag (device) and ep_h_ag (pinned), both kAgTotal words.
+constexpr uint32_t kAgWordsMax = 512 + 16 + 4;         // counts[E], tokens[R], T, status, pad
+constexpr uint32_t kAgRecv = kAgWordsMax;              // [world][W]
+constexpr uint32_t kAgBar = kAgRecv + 16 * kAgWordsMax;  // barrier: send [1], receive [16]
+constexpr uint32_t kHxWords = 4 + 3 * 16;              // status, pad, three 64-byte IPC handles
+constexpr uint32_t kAgHx = kAgBar + 32;                // handles: send [kHxWords], receive [16][..]
+constexpr uint32_t kAgHost = kAgHx + 17 * kHxWords;    // pinned only: T, status, barrier words
+constexpr uint32_t kAgTotal = kAgHost + 8;
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+inline uint32_t ep_ag_words(uint32_t E, int R) { return (E + static_cast<uint32_t>(R) + 2 + 3) & ~3u; }
+
 void release_ep(tsg_ctx ctx) {
   if (ctx->nccl_comm && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(ctx->nccl_comm));
   ctx->nccl_comm = nullptr;
+  close_peer_views(ctx);
+  for (int b = 0; b < kEpBufs; ++b) {
+    if (ctx->ep_buf[b]) cudaFree(ctx->ep_buf[b]);
+    ctx->ep_buf[b] = nullptr;
+    ctx->ep_buf_elems[b] = 0;
+  }
+  for (void* p : {static_cast<void*>(ctx->ep_ag), static_cast<void*>(ctx->ep_tile_out),
+                  static_cast<void*>(ctx->ep_ptiles), static_cast<void*>(ctx->ep_slots)})
+    if (p) cudaFree(p);
+  if (ctx->ep_h_ag) cudaFreeHost(ctx->ep_h_ag);
+  if (ctx->ep_h_tile_out) cudaFreeHost(ctx->ep_h_tile_out);
+  if (ctx->ep_h_ptiles) cudaFreeHost(ctx->ep_h_ptiles);
+  ctx->ep_ptiles = ctx->ep_h_ptiles = nullptr;
+  ctx->ep_pntiles = nullptr;
+  ctx->ep_ptiles_cap = 0;
+  ctx->ep_ag = ctx->ep_h_ag = nullptr;
+  ctx->ep_tile_out = ctx->ep_h_tile_out = nullptr;
+  ctx->ep_slots = nullptr;
+  ctx->ep_slots_cap = 0;
+  if (ctx->ep_ev_ok)
+    for (cudaEvent_t& e : ctx->ep_ev) cudaEventDestroy(e);
+  ctx->ep_ev_ok = false;
   for (void* p : {static_cast<void*>(ctx->ep_rows), static_cast<void*>(ctx->ep_act),
                   static_cast<void*>(ctx->ep_out), static_cast<void*>(ctx->ep_ret),
                   static_cast<void*>(ctx->ep_counts_recv), static_cast<void*>(ctx->ep_tiles)})
@@ -839,6 +916,11 @@ tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char* name, int64_t value) {
   }
   else if (n == "programmatic_launch") ctx->allow_pdl = value != 0;
   else if (n == "gemv_max_tokens") ctx->gemv_max_tokens = static_cast<uint32_t>(value < 0 ? 0 : value);
+  else if (n == "ep_transport") {
+    // every rank of a group must pass the same value before its next call
+    if (value != 0 && value != 1) return fail(ctx, TSG_ERR_INVALID_ARG, "ep_transport is 0 or 1");
+    ctx->ep_transport = static_cast<int>(value);
+  }
   else if (n == "debug_phase_stamps")
     ctx->stamps = reinterpret_cast<unsigned long long*>(static_cast<uintptr_t>(value));
   else return fail(ctx, TSG_ERR_INVALID_ARG, "unknown option " + n);
@@ -1671,13 +1753,452 @@ tsg_status tsg_ep_init(tsg_ctx ctx, const void* unique_id, int rank, int world) 
                                     cudaHostAllocDefault), "cudaHostAlloc");
   }
   if (world > 1024) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "at most 1024 ranks");
+  if (!ctx->ep_ag) {
+    TSG_CUDA_TRY(ctx, cudaMalloc(&ctx->ep_ag, kAgTotal * sizeof(uint32_t)), "cudaMalloc");
+    TSG_CUDA_TRY(ctx, cudaMemset(ctx->ep_ag, 0, kAgTotal * sizeof(uint32_t)), "cudaMemset");
+    TSG_CUDA_TRY(ctx, cudaHostAlloc(&ctx->ep_h_ag, kAgTotal * sizeof(uint32_t), cudaHostAllocDefault),
+                 "cudaHostAlloc");
+  }
+  if (!ctx->ep_ev_ok) {
+    bool ok = true;
+    for (cudaEvent_t& e : ctx->ep_ev) ok = ok && cudaEventCreate(&e) == cudaSuccess;
+    TSG_CUDA_TRY(ctx, ok ? cudaSuccess : cudaErrorMemoryAllocation, "cudaEventCreate");
+    ctx->ep_ev_ok = true;
+  }
   ncclComm_t comm = nullptr;
   TSG_NCCL_TRY(ctx, n.comm_init_rank(&comm, world, id, rank), "ncclCommInitRank");
   ctx->nccl_comm = comm;
   ctx->ep_rank = rank;
   ctx->ep_world = world;
+  for (std::vector<void*>& v : ctx->ep_peer) v.assign(world, nullptr);
+  for (std::vector<size_t>& c : ctx->ep_caps) c.assign(world, 0);
   return TSG_OK;
 }
+
+}  // extern "C"
+
+namespace {
+
+// The peer-memory transport of tsg_ep_moe_block_forward, after its local
+// phase (routing and sorting; the per-expert counts are in ep_ag's send
+// words).  One all-gather carries every rank's counts, token count and
+// status; from them every rank computes the same plan for all ranks -- the
+// pair runs, where each run lands in its owner's receive buffer, and every
+// buffer's needed capacity -- so a growth of any buffer is decided alike
+// everywhere.  Then: this rank's kernel writes its pair rows straight into
+// the owners' receive buffers (peer stores over NVLink), one barrier, the
+// owner's grouped contraction writes each output row straight into the
+// token's rank's return buffer from the GEMM2 epilogue, one barrier, and the
+// combine reads them in this rank's sorted order.  No host round trip after
+// the counts; no allocation unless a capacity grows.
+tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
+                           uint32_t hidden_stride, uint32_t T, const float* residual, void* y,
+                           uint32_t y_stride, tsg_dtype y_dtype, tsg_status local,
+                           std::string local_msg) {
+  const int R = ctx->ep_world, me = ctx->ep_rank;
+  const uint32_t E = L->desc.num_experts, K = L->desc.top_k, D = L->desc.d, F = L->desc.f;
+  const uint32_t El = E / static_cast<uint32_t>(R);
+  const uint32_t P = T * K;
+  const bool sh = L->has_shared != 0;
+  const NcclApi& n = nccl();
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl_comm);
+  cudaStream_t s = ctx->stream;
+  RouteBuffers& rb = ctx->rb;
+  const uint32_t W = ep_ag_words(E, R);  // words per rank: counts[E], tokens[R], T, status
+  uint32_t* ag_send = ctx->ep_ag;
+  uint32_t* ag_recv = ctx->ep_ag + kAgRecv;
+  uint32_t* bar_send = ctx->ep_ag + kAgBar;
+  uint32_t* bar_recv = bar_send + 1;
+  uint32_t* hx_send = ctx->ep_ag + kAgHx;
+  uint32_t* hx_recv = hx_send + kHxWords;
+  uint32_t* h = ctx->ep_h_ag;
+  auto ev = [&](int i) {
+    if (ctx->ep_ev_ok) cudaEventRecord(ctx->ep_ev[i], s);
+  };
+  auto note = [&](tsg_status st) {
+    if (local == TSG_OK && st != TSG_OK) {
+      local = st;
+      local_msg = ctx->last_error;
+    }
+  };
+  auto nccl_abort = [&](ncclResult_t r, const char* where) {
+    if (n.comm_abort) n.comm_abort(comm);
+    else n.comm_destroy(comm);
+    ctx->nccl_comm = nullptr;
+    close_peer_views(ctx);
+    return nccl_fail(ctx, r, where);
+  };
+#define EPP_NCCL(expr, where)                               \
+  do {                                                      \
+    const ncclResult_t r__ = (expr);                        \
+    if (r__ != ncclSuccess) return nccl_abort(r__, where);  \
+  } while (0)
+  // a barrier whose word carries this rank's status; with `read`, the host
+  // waits for it and learns whether every rank was fine (each barrier
+  // stages its word in its own pinned slot, kAgHost + 2 .., since the host
+  // does not wait between them)
+  auto barrier = [&](int slot, bool ok_local, bool read, bool* all_ok,
+                     int* first_bad) -> tsg_status {
+    h[kAgHost + slot] = ok_local ? 1u : 0u;
+    if (cudaMemcpyAsync(bar_send, &h[kAgHost + slot], 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
+      note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: barrier word"));
+    EPP_NCCL(n.all_gather(bar_send, bar_recv, 1, ncclUint32, comm, s), "ncclAllGather(barrier)");
+    if (!read) return TSG_OK;
+    uint32_t* hb = h + kAgBar;
+    if (cudaMemcpyAsync(hb, bar_recv, R * 4u, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return nccl_abort(ncclSystemError, "expert-parallel barrier readback");
+    *all_ok = true;
+    for (int q = 0; q < R; ++q)
+      if (hb[q] != 1u) {
+        *all_ok = false;
+        if (*first_bad < 0) *first_bad = q;
+      }
+    return TSG_OK;
+  };
+
+  // ---- agreement 1: every rank's counts, token count and status ----
+  h[kAgHost] = T;
+  h[kAgHost + 1] = local == TSG_OK ? 1u : 0u;
+  if (cudaMemcpyAsync(ag_send + E + R, &h[kAgHost], 8, cudaMemcpyHostToDevice, s) != cudaSuccess)
+    note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: count words"));
+  ev(1);
+  EPP_NCCL(n.all_gather(ag_send, ag_recv, W, ncclUint32, comm, s), "ncclAllGather(counts)");
+  if (cudaMemcpyAsync(h, ag_recv, static_cast<size_t>(R) * W * 4u, cudaMemcpyDeviceToHost, s) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return nccl_abort(ncclSystemError, "expert-parallel count readback");
+  int first_bad = -1;
+  for (int q = 0; q < R && first_bad < 0; ++q)
+    if (h[q * W + E + R + 1] != 1u) first_bad = q;
+  if (local != TSG_OK) return fail(ctx, local, local_msg);
+  if (first_bad >= 0)
+    return fail(ctx, TSG_ERR_NCCL, "expert-parallel: rank " + std::to_string(first_bad) +
+                                       " failed before the row exchange (its own call reports why)");
+
+  // ---- the plan, the same on every rank ----
+  // snd[q][o]: pairs q sends to o, at soff[q][o] of q's sorted order, landing
+  // at rpo[o][q] of o's received pairs; tok[q][o]: token rows q sends to o,
+  // at rro[o][q] of o's received rows
+  std::vector<uint32_t> M(h, h + static_cast<size_t>(R) * W);
+  const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
+  std::vector<uint32_t> Tq(R), snd(R * R), soff(R * R), rpo(R * R), tok(R * R), rro(R * R);
+  std::vector<uint32_t> recv_pairs(R), recv_rows(R);
+  std::vector<size_t> need[6];
+  for (std::vector<size_t>& v : need) v.assign(R, 0);
+  bool sums_ok = true;
+  for (int q = 0; q < R; ++q) {
+    Tq[q] = M[q * W + E + R];
+    uint32_t off = 0;
+    for (int o = 0; o < R; ++o) {
+      uint64_t c = 0;
+      for (uint32_t j = 0; j < El; ++j) c += M[q * W + o * El + j];
+      snd[q * R + o] = static_cast<uint32_t>(c);
+      soff[q * R + o] = off;
+      off += static_cast<uint32_t>(c);
+      tok[q * R + o] = M[q * W + E + o];
+      if (tok[q * R + o] > Tq[q] || tok[q * R + o] > c) sums_ok = false;
+    }
+    if (static_cast<uint64_t>(off) != static_cast<uint64_t>(Tq[q]) * K) sums_ok = false;
+  }
+  if (!sums_ok)  // (every rank sees the same counts and returns here)
+    return fail(ctx, TSG_ERR_CUDA, "expert-parallel: pair counts do not add up");
+  for (int o = 0; o < R; ++o) {
+    uint64_t acc = 0, rows = 0, tiles = 0;
+    for (int q = 0; q < R; ++q) {
+      rpo[o * R + q] = static_cast<uint32_t>(acc);
+      rro[o * R + q] = static_cast<uint32_t>(rows);
+      acc += snd[q * R + o];
+      rows += tok[q * R + o];
+      for (uint32_t j = 0; j < El; ++j) tiles += (M[q * W + o * El + j] + tr - 1) / tr;
+    }
+    if (acc > UINT32_MAX / 2) sums_ok = false;
+    recv_pairs[o] = static_cast<uint32_t>(acc);
+    recv_rows[o] = static_cast<uint32_t>(rows);
+    const size_t xrows = acc + (sh ? Tq[o] : 0u);
+    need[kEpXp][o] = xrows * D;
+    need[kEpAct][o] = xrows * F;
+    need[kEpRet][o] = (static_cast<size_t>(Tq[o]) * K + (sh ? Tq[o] : 0u)) * D;
+    need[kEpRows][o] = rows * D;
+    need[kEpMap][o] = acc;
+    need[5][o] = tiles + (sh ? (Tq[o] + tr - 1) / tr : 0u);
+  }
+  if (!sums_ok) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "expert-parallel: too many pairs");
+
+  // ---- growth (decided alike on every rank): unmap, barrier, replace what
+  // is short, publish the handles of the buffers peers write, map the
+  // peers', agree ----
+  bool grow_all = false;
+  for (int b = 0; b < 6; ++b)
+    for (int r = 0; r < R; ++r)
+      if (need[b][r] > ctx->ep_caps[b][r]) grow_all = true;
+  if (grow_all) {
+    std::vector<size_t> cap[6];
+    for (int b = 0; b < 6; ++b) {
+      cap[b].resize(R);
+      for (int r = 0; r < R; ++r) {
+        const size_t nd = need[b][r], c = ctx->ep_caps[b][r];
+        cap[b][r] = nd > c ? std::max<size_t>(nd + nd / 4, b == 5 ? 256u : 1u << 16) : c;
+      }
+    }
+    close_peer_views(ctx);
+    bool all_ok = false;
+    first_bad = -1;
+    {
+      const tsg_status st = barrier(4, true, true, &all_ok, &first_bad);
+      if (st != TSG_OK) return st;
+    }
+    // no rank maps another's buffers now
+    bool ok = true;
+    for (int b = 0; b < kEpBufs && ok; ++b) {
+      if (cap[b][me] <= ctx->ep_buf_elems[b] && ctx->ep_buf[b]) continue;
+      if (ctx->ep_buf[b]) cudaFree(ctx->ep_buf[b]);
+      ctx->ep_buf[b] = nullptr;
+      ctx->ep_buf_elems[b] = 0;
+      ok = cudaMalloc(&ctx->ep_buf[b], cap[b][me] * kEpElemBytes[b]) == cudaSuccess;
+      if (ok) ctx->ep_buf_elems[b] = cap[b][me];
+    }
+    if (ok && (!ctx->ep_ptiles || ctx->ep_ptiles_cap < cap[5][me] + 1)) {
+      for (void* p : {static_cast<void*>(ctx->ep_ptiles), static_cast<void*>(ctx->ep_tile_out)})
+        if (p) cudaFree(p);
+      for (void* p : {static_cast<void*>(ctx->ep_h_ptiles), static_cast<void*>(ctx->ep_h_tile_out)})
+        if (p) cudaFreeHost(p);
+      ctx->ep_ptiles = ctx->ep_h_ptiles = nullptr;
+      ctx->ep_tile_out = ctx->ep_h_tile_out = nullptr;
+      ctx->ep_ptiles_cap = 0;
+      const size_t c = cap[5][me] + 1;
+      ok = cudaMalloc(&ctx->ep_ptiles, (c + 1) * sizeof(RowTile)) == cudaSuccess &&
+           cudaHostAlloc(&ctx->ep_h_ptiles, (c + 1) * sizeof(RowTile), cudaHostAllocDefault) ==
+               cudaSuccess &&
+           cudaMalloc(&ctx->ep_tile_out, c * sizeof(unsigned long long)) == cudaSuccess &&
+           cudaHostAlloc(&ctx->ep_h_tile_out, c * sizeof(unsigned long long),
+                         cudaHostAllocDefault) == cudaSuccess;
+      if (ok) ctx->ep_ptiles_cap = c;
+    }
+    if (!ok) cudaGetLastError();  // (reported through the handle exchange)
+    // publish: status, pad, then a handle per buffer that peers write
+    uint32_t* hs = h + kAgHx;
+    std::memset(hs, 0, kHxWords * 4);
+    for (int b = 0, k = 0; b < kEpBufs && ok; ++b) {
+      if (!kEpShared[b]) continue;
+      cudaIpcMemHandle_t hd;
+      ok = cudaIpcGetMemHandle(&hd, ctx->ep_buf[b]) == cudaSuccess;
+      std::memcpy(hs + 4 + 16 * k++, &hd, 64);
+    }
+    hs[0] = ok ? 1u : 0u;
+    if (cudaMemcpyAsync(hx_send, hs, kHxWords * 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
+      return nccl_abort(ncclSystemError, "expert-parallel handle staging");
+    EPP_NCCL(n.all_gather(hx_send, hx_recv, kHxWords, ncclUint32, comm, s),
+             "ncclAllGather(handles)");
+    uint32_t* hrv = h + kAgHx + kHxWords;
+    if (cudaMemcpyAsync(hrv, hx_recv, static_cast<size_t>(R) * kHxWords * 4,
+                        cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return nccl_abort(ncclSystemError, "expert-parallel handle readback");
+    first_bad = -1;
+    for (int q = 0; q < R && first_bad < 0; ++q)
+      if (hrv[q * kHxWords] != 1u) first_bad = q;
+    if (first_bad >= 0)
+      return fail(ctx, TSG_ERR_CUDA, "expert-parallel: rank " + std::to_string(first_bad) +
+                                         " could not allocate its exchange buffers");
+    // map the peers' buffers (this rank's own are used directly)
+    for (int q = 0; q < R; ++q)
+      for (int b = 0, k = 0; b < kEpBufs; ++b) {
+        if (q == me || !kEpShared[b]) {
+          ctx->ep_peer[b][q] = q == me ? ctx->ep_buf[b] : nullptr;
+          continue;
+        }
+        cudaIpcMemHandle_t hd;
+        std::memcpy(&hd, hrv + q * kHxWords + 4 + 16 * k++, 64);
+        void* ptr = nullptr;
+        if (ok) ok = cudaIpcOpenMemHandle(&ptr, hd, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        ctx->ep_peer[b][q] = ok ? ptr : nullptr;
+      }
+    if (!ok) cudaGetLastError();  // (reported through the agreement)
+    first_bad = -1;
+    {
+      const tsg_status st = barrier(5, ok, true, &all_ok, &first_bad);
+      if (st != TSG_OK) return st;
+    }
+    if (!all_ok) {
+      close_peer_views(ctx);
+      return fail(ctx, TSG_ERR_CUDA, "expert-parallel: rank " + std::to_string(first_bad) +
+                                         " could not map its peers' buffers");
+    }
+    for (int b = 0; b < 6; ++b) ctx->ep_caps[b] = cap[b];
+  }
+  __half* xp = static_cast<__half*>(ctx->ep_buf[kEpXp]);
+  __half* act = static_cast<__half*>(ctx->ep_buf[kEpAct]);
+  __half* ret = static_cast<__half*>(ctx->ep_buf[kEpRet]);
+  const __half* rows_in = static_cast<const __half*>(ctx->ep_buf[kEpRows]);
+  const uint32_t* map_in = static_cast<const uint32_t*>(ctx->ep_buf[kEpMap]);
+
+  // ---- this rank's row tiles, each with its rows' destination ----
+  const uint32_t rows_here = recv_pairs[me] + (sh ? T : 0u);
+  RowTile* ht = ctx->ep_h_ptiles;
+  unsigned long long* hto = ctx->ep_h_tile_out;
+  uint32_t n_tiles = 0;
+  for (int q = 0; q < R && local == TSG_OK; ++q) {
+    uint32_t row = rpo[me * R + q];    // in this rank's received pairs
+    uint32_t back = soff[q * R + me];  // in q's sorted order
+    __half* qret = static_cast<__half*>(ctx->ep_peer[kEpRet][q]);
+    for (uint32_t j = 0; j < El; ++j) {
+      const uint32_t c = M[q * W + me * El + j];
+      for (uint32_t b = 0; b < c && local == TSG_OK; b += tr) {
+        const uint32_t rows = std::min(tr, c - b);
+        if (n_tiles + 1 >= ctx->ep_ptiles_cap ||
+            static_cast<size_t>(back + b + rows) * D > ctx->ep_caps[kEpRet][q]) {
+          note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: tile plan exceeds a buffer"));
+          break;
+        }
+        ht[n_tiles] = {j, row + b, rows, 0};
+        hto[n_tiles] = reinterpret_cast<unsigned long long>(qret + static_cast<size_t>(back + b) * D);
+        ++n_tiles;
+      }
+      row += c;
+      back += c;
+    }
+  }
+  for (uint32_t b = 0; sh && b < T && local == TSG_OK; b += tr) {
+    const uint32_t rows = std::min(tr, T - b);
+    if (n_tiles + 1 >= ctx->ep_ptiles_cap) {
+      note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: tile plan exceeds a buffer"));
+      break;
+    }
+    ht[n_tiles] = {El, recv_pairs[me] + b, rows, 0};
+    hto[n_tiles] = reinterpret_cast<unsigned long long>(ret + static_cast<size_t>(P + b) * D);
+    ++n_tiles;
+  }
+  if (local != TSG_OK) n_tiles = 0;
+  ht[ctx->ep_ptiles_cap].expert = n_tiles;  // the count rides after the tiles
+  ctx->ep_pntiles = &ctx->ep_ptiles[ctx->ep_ptiles_cap].expert;
+  auto cuda_note = [&](cudaError_t e, const char* where) {
+    if (e != cudaSuccess) note(cuda_fail(ctx, e, where));
+  };
+  if (n_tiles) {
+    cuda_note(cudaMemcpyAsync(ctx->ep_ptiles, ht, n_tiles * sizeof(RowTile), cudaMemcpyHostToDevice,
+                              s),
+              "tiles");
+    cuda_note(cudaMemcpyAsync(ctx->ep_tile_out, hto, n_tiles * sizeof(unsigned long long),
+                              cudaMemcpyHostToDevice, s),
+              "tiles");
+  }
+  cuda_note(cudaMemcpyAsync(ctx->ep_pntiles, &ht[ctx->ep_ptiles_cap].expert, 4,
+                            cudaMemcpyHostToDevice, s),
+            "tiles");
+  // this rank's shared-expert rows (and the shared gate's dots) after the
+  // pairs it receives
+  if (sh && T > 0 && local == TSG_OK) {
+    const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(E) * D : nullptr;
+    cuda_note(launch_gather_rows_gate(static_cast<const uint16_t*>(hidden), hidden_stride,
+                                      rb.inv_rms, rb.sorted_pairs, 0, static_cast<int>(T),
+                                      static_cast<int>(D), 1,
+                                      xp + static_cast<size_t>(recv_pairs[me]) * D, gate_w,
+                                      rb.gate_raw, s),
+              "shared rows");
+  }
+  ev(2);
+  // ---- dispatch: each token row once to every owner of one of its
+  // experts, and each pair's row index, into the owners' buffers ----
+  if (P > 0 && local == TSG_OK) {
+    EpDispatch d{};
+    d.x = static_cast<const uint16_t*>(hidden);
+    d.x_stride = hidden_stride;
+    d.inv_rms = rb.inv_rms;
+    d.sorted_pairs = rb.sorted_pairs;
+    d.slots = ctx->ep_slots;
+    d.P = static_cast<int>(P);
+    d.T = static_cast<int>(T);
+    d.D = static_cast<int>(D);
+    d.experts_per_rank = static_cast<int>(El);
+    d.world = R;
+    for (int o = 0; o < R; ++o) {
+      d.rows[o] = static_cast<__half*>(ctx->ep_peer[kEpRows][o]);
+      d.map[o] = static_cast<uint32_t*>(ctx->ep_peer[kEpMap][o]);
+      d.row0[o] = rro[o * R + me];
+      d.row_cap[o] = static_cast<uint32_t>(std::min<size_t>(ctx->ep_caps[kEpRows][o] / D, UINT32_MAX));
+      d.n_rows[o] = tok[me * R + o];
+      d.map0[o] = rpo[o * R + me];
+      d.map_cap[o] = static_cast<uint32_t>(std::min<size_t>(ctx->ep_caps[kEpMap][o], UINT32_MAX));
+      d.send_off[o] = soff[me * R + o];
+      d.send_cnt[o] = snd[me * R + o];
+    }
+    d.err = rb.err;
+    cuda_note(launch_ep_dispatch(d, s), "dispatch");
+  }
+  {
+    bool all_ok = false;
+    const tsg_status st = barrier(2, local == TSG_OK, false, &all_ok, &first_bad);
+    if (st != TSG_OK) return st;
+  }
+  ev(3);
+  // ---- the received pairs' rows, in (source rank, expert) runs ----
+  if (local == TSG_OK)
+    cuda_note(launch_ep_expand(rows_in,
+                               static_cast<uint32_t>(std::min<size_t>(ctx->ep_caps[kEpRows][me] / D,
+                                                                      UINT32_MAX)),
+                               map_in, static_cast<int>(recv_pairs[me]), static_cast<int>(D), xp,
+                               rb.err, s),
+              "expand");
+  ev(4);
+  // ---- the grouped contraction; GEMM2 writes each row to its token's rank ----
+  if (n_tiles && local == TSG_OK) {
+    QmmParams qp{};
+    qp.D = static_cast<int>(D);
+    qp.F = static_cast<int>(F);
+    qp.E = static_cast<int>(El);
+    qp.act = static_cast<int>(L->desc.activation);
+    qp.n_rows_total = static_cast<int>(rows_here);
+    qp.experts = expert_set(L);
+    qp.row_tiles = ctx->ep_ptiles;
+    qp.n_row_tiles = ctx->ep_pntiles;
+    qp.xp = xp;
+    qp.act_buf = act;
+    qp.partials = ret;
+    qp.tile_out = ctx->ep_tile_out;
+    qp.err = rb.err;
+    qp.num_sms = ctx->num_sms;
+    cuda_note(launch_qmm_gate_up(qp, s), "qmm gate/up");
+    ev(5);
+    if (local == TSG_OK) cuda_note(launch_qmm_down(qp, s), "qmm down");
+  } else {
+    ev(5);
+  }
+  ev(6);
+  {
+    bool all_ok = false;
+    const tsg_status st = barrier(3, local == TSG_OK, false, &all_ok, &first_bad);
+    if (st != TSG_OK) return st;
+  }
+#undef EPP_NCCL
+  ev(7);
+  if (local != TSG_OK) return fail(ctx, local, local_msg);
+  // combine this rank's tokens, ranks in order (as on one GPU)
+  if (T > 0) {
+    CombineParams cp{};
+    cp.T = static_cast<int>(T);
+    cp.D = static_cast<int>(D);
+    cp.K = static_cast<int>(K);
+    cp.has_shared = L->has_shared;
+    cp.E = static_cast<int>(E);
+    cp.partials = ret;
+    cp.pair_pos = rb.pair_pos;
+    cp.weights = rb.weights;
+    cp.gate_raw = L->has_gate ? rb.gate_raw : nullptr;
+    cp.inv_rms = rb.inv_rms;
+    cp.residual = residual;
+    cp.y = y;
+    cp.y_stride = y_stride;
+    cp.y_f32 = y_dtype == TSG_DTYPE_F32 ? 1 : 0;
+    TSG_CUDA_TRY(ctx, launch_combine(cp, s), "combine");
+  }
+  ev(8);
+  return TSG_OK;
+}
+
+}  // namespace
+
+extern "C" {
 
 // Every rank of the group takes the same collective steps in the same order,
 // whatever fails where: a local failure (bad arguments, a launch, an
@@ -1747,6 +2268,12 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
     return TSG_OK;
   };
 
+  const bool peer = ctx->ep_transport == 1;
+  if (peer && R > kEpMaxRanks)  // (the same on every rank: all return here)
+    return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "peer transport: at most 16 ranks");
+  if (peer && ctx->ep_ev_ok) cudaEventRecord(ctx->ep_ev[0], s);
+  uint32_t* csend = peer ? ctx->ep_ag : counts_send;
+
   // ---- phase 1 (local): checks, routing, sorting, the rows to send ----
   tsg_status local = TSG_OK;
   std::string local_msg;
@@ -1782,21 +2309,37 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
       TSG_CUDA_TRY(ctx, launch_router_prefill(p, rb, s), "router");
       TSG_CUDA_TRY(ctx, launch_permute(p, rb, nullptr, s), "permute");
       const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(E) * D : nullptr;
-      TSG_CUDA_TRY(ctx,
-                   launch_gather_rows_gate(static_cast<const uint16_t*>(hidden), hidden_stride,
-                                           rb.inv_rms, rb.sorted_pairs, static_cast<int>(P),
-                                           static_cast<int>(T), static_cast<int>(D), L->has_shared,
-                                           ctx->xp, gate_w, rb.gate_raw, s),
-                   "gather rows");
-      TSG_CUDA_TRY(ctx, cudaMemcpyAsync(counts_send, rb.counts, E * 4u, cudaMemcpyDeviceToDevice, s),
+      if (!peer)  // (the peer transport converts the rows as it sends them)
+        TSG_CUDA_TRY(ctx,
+                     launch_gather_rows_gate(static_cast<const uint16_t*>(hidden), hidden_stride,
+                                             rb.inv_rms, rb.sorted_pairs, static_cast<int>(P),
+                                             static_cast<int>(T), static_cast<int>(D),
+                                             L->has_shared, ctx->xp, gate_w, rb.gate_raw, s),
+                     "gather rows");
+      TSG_CUDA_TRY(ctx, cudaMemcpyAsync(csend, rb.counts, E * 4u, cudaMemcpyDeviceToDevice, s),
                    "counts");
+      if (peer) {
+        // each token's slot among the rows sent to each owner, and the
+        // number of rows per owner beside the counts
+        TSG_CUDA_TRY(ctx, grow(&ctx->ep_slots, &ctx->ep_slots_cap, static_cast<size_t>(R) * T),
+                     "cudaMalloc");
+        TSG_CUDA_TRY(ctx,
+                     launch_ep_owner_slots(rb.ids, static_cast<int>(T), static_cast<int>(K),
+                                           static_cast<int>(El), R, ctx->ep_slots, csend + E, s),
+                     "owner slots");
+      }
     } else {
-      TSG_CUDA_TRY(ctx, cudaMemsetAsync(counts_send, 0, E * 4u, s), "memset");
+      TSG_CUDA_TRY(ctx, cudaMemsetAsync(csend, 0, (E + (peer ? R : 0)) * 4u, s), "memset");
     }
     return TSG_OK;
   };
   if (local == TSG_OK) note(route());
-  if (local != TSG_OK) cudaMemsetAsync(counts_send, 0, 512 * 4u, s);  // (what is sent is not read)
+  if (local != TSG_OK) cudaMemsetAsync(csend, 0, 512 * 4u, s);  // (what is sent is not read)
+  if (peer) {
+    const tsg_status st = ep_peer_forward(ctx, L, hidden, hidden_stride, T, residual, y, y_stride,
+                                          y_dtype, local, local_msg);
+    return st;
+  }
 
   // ---- agreement 1, with the per-expert pair counts to their owners ----
   const uint32_t Elx = El ? El : E / static_cast<uint32_t>(R);  // counts each peer expects
@@ -1994,6 +2537,18 @@ tsg_status tsg_ep_moe_block_forward(tsg_ctx ctx, tsg_moe_layer L, uint32_t exper
     cp.y_stride = y_stride;
     cp.y_f32 = y_dtype == TSG_DTYPE_F32 ? 1 : 0;
     TSG_CUDA_TRY(ctx, launch_combine(cp, s), "combine");
+  }
+  return TSG_OK;
+}
+
+tsg_status tsg_ep_phase_ms(tsg_ctx ctx, float* ms, int n) {
+  if (!ctx || (!ms && n > 0)) return fail(ctx, TSG_ERR_INVALID_ARG, "null argument");
+  if (!ctx->ep_ev_ok) return fail(ctx, TSG_ERR_INVALID_ARG, "tsg_ep_init has not been called");
+  TSG_CUDA_TRY(ctx, cudaEventSynchronize(ctx->ep_ev[8]), "phase events");
+  for (int i = 0; i < n && i < 8; ++i) {
+    float t = 0.0f;
+    TSG_CUDA_TRY(ctx, cudaEventElapsedTime(&t, ctx->ep_ev[i], ctx->ep_ev[i + 1]), "phase events");
+    ms[i] = t;
   }
   return TSG_OK;
 }

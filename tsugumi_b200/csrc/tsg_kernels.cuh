@@ -128,6 +128,37 @@ cudaError_t launch_gather_rows_gate(const uint16_t* x, uint32_t x_stride, const 
                                     int append_tokens, __half* xp, const float* gate_w,
                                     float* gate_raw, cudaStream_t s, int frag_order = 0);
 
+// Expert parallelism over peer memory.  A token is sent once to each rank
+// that owns at least one of its experts: slots[o][t] is the token's index
+// among the tokens this rank sends to owner o (token order), kEpNoSlot when
+// none of its experts is on o; counts[o] the number of such tokens.
+constexpr int kEpMaxRanks = 16;
+constexpr uint32_t kEpNoSlot = 0xFFFFFFFFu;
+cudaError_t launch_ep_owner_slots(const uint32_t* ids, int T, int K, int experts_per_rank,
+                                  int world, uint32_t* slots, uint32_t* counts, cudaStream_t s);
+// The dispatch writes the token's fp16 row (gather_rows_kernel's conversion)
+// to row row0[o] + slot of rows[o], and for pair i of this rank's sorted
+// order, owned by o, the row's index to entry map0[o] + (i - send_off[o]) of
+// map[o] -- the owner's buffers, in peer or local memory.
+struct EpDispatch {
+  const uint16_t* x;
+  uint32_t x_stride;
+  const float* inv_rms;
+  const Pair* sorted_pairs;
+  const uint32_t* slots;  // [world][T]
+  int P, T, D, experts_per_rank, world;
+  __half* rows[kEpMaxRanks];
+  uint32_t* map[kEpMaxRanks];
+  uint32_t row0[kEpMaxRanks], row_cap[kEpMaxRanks], n_rows[kEpMaxRanks];  // rows: first, capacity, sent
+  uint32_t map0[kEpMaxRanks], map_cap[kEpMaxRanks];
+  uint32_t send_off[kEpMaxRanks], send_cnt[kEpMaxRanks];  // this rank's pairs to o
+  uint32_t* err;
+};
+cudaError_t launch_ep_dispatch(const EpDispatch& d, cudaStream_t s);
+// The owner's expansion: xp[i] = rows[map[i]] for the n pairs it received.
+cudaError_t launch_ep_expand(const __half* rows, uint32_t rows_cap, const uint32_t* map, int n,
+                             int D, __half* xp, uint32_t* err, cudaStream_t s);
+
 // decode.cu
 struct DecodeParams {
   int T, D, F, E, K, act, has_shared;
@@ -211,6 +242,10 @@ struct QmmParams {
   const __half* xp;      // [rows, D] fp16 (GEMM1 input)
   __half* act_buf;       // [rows, F] fp16 (GEMM1 output, GEMM2 input)
   __half* partials;      // [rows, D] fp16 (GEMM2 output)
+  // optional: per row tile, where GEMM2 writes the tile's rows instead of
+  // partials (row r of the tile at tile_out[tile] + r * D; expert
+  // parallelism points these into the token's rank's memory)
+  const unsigned long long* tile_out;
   uint32_t* err;
   int num_sms;
 };

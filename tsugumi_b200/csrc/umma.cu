@@ -106,6 +106,7 @@ struct QArgs {
   uint32_t sc_bytes;  // one scale buffer, 128-byte aligned
   uint32_t c_off, s_off;  // code ring / scale buffers, from the aligned smem base
   __half* out;
+  const unsigned long long* tile_out;  // mode 1, optional: per row tile, its rows' destination
   uint32_t* err;
 };
 
@@ -124,7 +125,7 @@ struct SmemQ {
 };
 
 struct WorkItem {
-  uint32_t expert, row_start, rows, wt;
+  uint32_t expert, row_start, rows, wt, tile;
   bool valid;
 };
 
@@ -134,6 +135,7 @@ TSG_DEV WorkItem work_item(const QArgs& a, uint32_t n_items, uint32_t idx) {
   if (!w.valid) return w;
   const uint32_t rt = idx / static_cast<uint32_t>(a.n_wt);
   w.wt = idx % static_cast<uint32_t>(a.n_wt);
+  w.tile = rt;
   const RowTile t = a.tiles[rt];
   w.expert = t.expert;
   w.row_start = t.row_start;
@@ -483,12 +485,13 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
           }
         } else {
           const uint32_t dcol = w.wt * 128u + static_cast<uint32_t>(q * 32 + lane);
+          __half* ob = a.tile_out ? reinterpret_cast<__half*>(a.tile_out[w.tile])
+                                  : a.out + static_cast<size_t>(w.row_start) * a.out_cols;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const uint32_t col = c0 + j;
             if (col < w.rows)
-              a.out[static_cast<size_t>(w.row_start + col) * a.out_cols + dcol] =
-                  __float2half_rn(__uint_as_float(r[j]));
+              ob[static_cast<size_t>(col) * a.out_cols + dcol] = __float2half_rn(__uint_as_float(r[j]));
           }
         }
       }
@@ -496,6 +499,9 @@ __global__ void __launch_bounds__(kThreadsQ, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.tmem_empty[acc]);
     }
+    // rows written into another rank's memory are visible there before the
+    // collective that follows this kernel
+    if (MODE == 1 && a.tile_out) __threadfence_system();
   }
 
   tc_fence_before_sync();
@@ -569,6 +575,7 @@ cudaError_t launch_qmm(const QmmParams& p, cudaStream_t s) {
   a.act = p.act;
   a.out_cols = MODE == 0 ? p.F : p.D;
   a.out = MODE == 0 ? p.act_buf : p.partials;
+  a.tile_out = MODE == 1 ? p.tile_out : nullptr;
   a.err = p.err;
 
   // token rows

@@ -88,3 +88,14 @@ class EPMoELayer(MoELayer):
             self.ctx.h, self.h, self.expert_first, _ptr(hidden), hidden.stride(0), T,
             _ptr(residual), _ptr(y), y.stride(0), dt), self.ctx.h)
         return y
+
+    PHASES = ("route", "exchange_plan", "dispatch", "expand", "gate_up", "down_return", "barrier",
+              "combine")
+
+    def phase_ms(self) -> dict:
+        """Device time of each phase of the context's last peer-transport
+        call (tsg_ep_phase_ms); waits for it."""
+        buf = (C.c_float * len(self.PHASES))()
+        check(self.ctx.lib.tsg_ep_phase_ms(self.ctx.h, C.cast(buf, C.c_void_p), len(self.PHASES)),
+              self.ctx.h)
+        return {k: float(v) for k, v in zip(self.PHASES, buf)}
