@@ -141,7 +141,11 @@ TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
  * num_sms x 8 uint64 the fused decode kernel fills with %globaltimer stamps
  * at its phase boundaries, or 0 for none), "ep_transport" (expert
  * parallelism: 1, the default, moves rows through peer memory; 0 through
- * NCCL all-to-all; every rank of a group sets the same value). */
+ * NCCL all-to-all; every rank of a group sets the same value) and
+ * "ep_return" (peer transport: 1, the default, runs the down contraction in
+ * one chunk per source rank and copies each finished chunk to its rank with
+ * the copy engines while the next computes; 0 lets the contraction's
+ * epilogue store the rows into the peers' buffers). */
 TSG_API tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char *name, int64_t value);
 /* Pre-allocates the workspace for up to max_tokens tokens of this layer's
  * shape, so later calls allocate nothing (required before stream capture). */
@@ -374,10 +378,10 @@ TSG_API tsg_status tsg_last_routing(tsg_ctx ctx, const uint32_t **ids, const flo
  * order -- the same arithmetic as one GPU, so the outputs are bit-equal.
  * With the peer transport (default, at most 16 ranks) a kernel stores each
  * token row once per owner rank straight into the owners' buffers over
- * NVLink (the owner expands them into pair rows), and the contraction's
- * epilogue stores each output row into its token's rank's buffer (buffers
- * mapped between the processes with CUDA IPC); NCCL carries the counts and
- * the barriers.  With "ep_transport" 0 NCCL all-to-all carries the rows.
+ * NVLink (the owner expands them into pair rows), and the expert outputs
+ * go back into the token's rank's buffer by copy engine, a chunk per source
+ * rank as the down contraction finishes it (buffers mapped between the
+ * processes with CUDA IPC); NCCL carries the counts and the barriers.  With "ep_transport" 0 NCCL all-to-all carries the rows.
  * NCCL (libnccl.so.2) is loaded when tsg_ep_init is first called. */
 #define TSG_EP_UNIQUE_ID_BYTES 128
 

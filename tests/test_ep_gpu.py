@@ -16,7 +16,7 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 ROOT = Path(__file__).resolve().parent.parent
-WORLD = 2
+WORLD = int(os.environ.get("TSG_EP_TEST_WORLD", "2"))
 CASES = [
     # config, tokens of rank 0 (rank r has 3r more), skew
     ("tiny", 16, None),
@@ -24,7 +24,9 @@ CASES = [
     ("qwen", 300, None),
     ("gemma_dense", 200, 1.1),
 ]
-TRANSPORTS = (1, 0)  # peer memory, NCCL all-to-all
+# (transport, return): peer memory with the outputs returned by the copy
+# engines, peer memory with GEMM2's epilogue storing them, NCCL all-to-all
+TRANSPORTS = ((1, 1), (1, 0), (0, 1))
 
 
 def _free_port() -> int:
@@ -53,8 +55,9 @@ def _rank_main(rank: int, port: int, q):
         ctx.set_option("gemv_max_tokens", 0)
         group = ep.ExpertParallelGroup.from_torch_distributed(ctx)
         msgs = []
-        for transport in TRANSPORTS:
+        for transport, ret in TRANSPORTS:
             ctx.set_option("ep_transport", transport)
+            ctx.set_option("ep_return", ret)
             for name, T0, skew in CASES:
                 t = device_layer_tensors(name, 4242, skew, dev)
                 full = tb.MoELayer(ctx, t)
@@ -70,7 +73,7 @@ def _rank_main(rank: int, port: int, q):
                 ctx.sync()
                 same = torch.equal(got, want) and torch.equal(got2, want)
                 diff = float((got - want).abs().max())
-                msgs.append((f"{name} transport {transport}", same, diff))
+                msgs.append((f"{name} transport {transport} return {ret}", same, diff))
                 if transport == 1:
                     ph = shard.phase_ms()
                     msgs.append((f"{name} phases", all(v >= 0 for v in ph.values()), 0.0))
@@ -86,7 +89,7 @@ def _rank_main(rank: int, port: int, q):
 
 def test_expert_parallel_matches_single_gpu_bit_for_bit():
     if torch.cuda.device_count() < WORLD:
-        pytest.skip("needs two GPUs")
+        pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")

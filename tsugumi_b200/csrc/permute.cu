@@ -478,7 +478,21 @@ __global__ void __launch_bounds__(256) ep_expand_kernel(const __half* rows, uint
   }
   const uint4* src = reinterpret_cast<const uint4*>(rows + static_cast<size_t>(r) * D);
   uint4* dst = reinterpret_cast<uint4*>(xp + static_cast<size_t>(i) * D);
-  for (int c = lane; c < D / 8; c += 32) dst[c] = src[c];
+  // eight 16-byte loads in flight per lane before their stores
+  const int n16 = D / 8;
+  for (int c0 = 0; c0 < n16; c0 += 256) {
+    uint4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = c0 + 32 * k + lane;
+      if (c < n16) v[k] = src[c];
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = c0 + 32 * k + lane;
+      if (c < n16) dst[c] = v[k];
+    }
+  }
 }
 
 }  // namespace

@@ -134,6 +134,13 @@ struct tsg_ctx_s {
   unsigned long long* ep_tile_out = nullptr;    // device [ep_ptiles_cap]: per tile, rows' destination
   unsigned long long* ep_h_tile_out = nullptr;  // pinned staging
   cudaEvent_t ep_ev[9] = {};           // phase boundaries of the last call (peer transport)
+  // the return through the copy engines (ep_return 1): GEMM2 runs in chunks,
+  // one per source rank, into local rows, and a second stream copies each
+  // finished chunk into its rank's buffer while the next chunk computes
+  int ep_return = 1;                   // 0: GEMM2's epilogue stores into the peers' buffers
+  cudaStream_t ep_copy = nullptr;
+  cudaEvent_t ep_chunk_ev[kEpMaxRanks + 1] = {};
+  bool ep_chunk_ok = false;
   bool ep_ev_ok = false;
 };
 
@@ -739,6 +746,12 @@ void release_ep(tsg_ctx ctx) {
   if (ctx->ep_ev_ok)
     for (cudaEvent_t& e : ctx->ep_ev) cudaEventDestroy(e);
   ctx->ep_ev_ok = false;
+  if (ctx->ep_chunk_ok) {
+    for (cudaEvent_t& e : ctx->ep_chunk_ev) cudaEventDestroy(e);
+    cudaStreamDestroy(ctx->ep_copy);
+  }
+  ctx->ep_copy = nullptr;
+  ctx->ep_chunk_ok = false;
   for (void* p : {static_cast<void*>(ctx->ep_rows), static_cast<void*>(ctx->ep_act),
                   static_cast<void*>(ctx->ep_out), static_cast<void*>(ctx->ep_ret),
                   static_cast<void*>(ctx->ep_counts_recv), static_cast<void*>(ctx->ep_tiles)})
@@ -916,6 +929,11 @@ tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char* name, int64_t value) {
   }
   else if (n == "programmatic_launch") ctx->allow_pdl = value != 0;
   else if (n == "gemv_max_tokens") ctx->gemv_max_tokens = static_cast<uint32_t>(value < 0 ? 0 : value);
+  else if (n == "ep_return") {
+    // every rank of a group sets the same value (it changes no collective)
+    if (value != 0 && value != 1) return fail(ctx, TSG_ERR_INVALID_ARG, "ep_return is 0 or 1");
+    ctx->ep_return = static_cast<int>(value);
+  }
   else if (n == "ep_transport") {
     // every rank of a group must pass the same value before its next call
     if (value != 0 && value != 1) return fail(ctx, TSG_ERR_INVALID_ARG, "ep_transport is 0 or 1");
@@ -1765,6 +1783,13 @@ tsg_status tsg_ep_init(tsg_ctx ctx, const void* unique_id, int rank, int world) 
     TSG_CUDA_TRY(ctx, ok ? cudaSuccess : cudaErrorMemoryAllocation, "cudaEventCreate");
     ctx->ep_ev_ok = true;
   }
+  if (!ctx->ep_chunk_ok) {
+    bool ok = cudaStreamCreateWithFlags(&ctx->ep_copy, cudaStreamNonBlocking) == cudaSuccess;
+    for (cudaEvent_t& e : ctx->ep_chunk_ev)
+      ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+    TSG_CUDA_TRY(ctx, ok ? cudaSuccess : cudaErrorMemoryAllocation, "copy stream");
+    ctx->ep_chunk_ok = true;
+  }
   ncclComm_t comm = nullptr;
   TSG_NCCL_TRY(ctx, n.comm_init_rank(&comm, world, id, rank), "ncclCommInitRank");
   ctx->nccl_comm = comm;
@@ -1966,10 +1991,10 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
       ctx->ep_ptiles = ctx->ep_h_ptiles = nullptr;
       ctx->ep_tile_out = ctx->ep_h_tile_out = nullptr;
       ctx->ep_ptiles_cap = 0;
-      const size_t c = cap[5][me] + 1;
-      ok = cudaMalloc(&ctx->ep_ptiles, (c + 1) * sizeof(RowTile)) == cudaSuccess &&
-           cudaHostAlloc(&ctx->ep_h_ptiles, (c + 1) * sizeof(RowTile), cudaHostAllocDefault) ==
-               cudaSuccess &&
+      const size_t c = cap[5][me] + 1;  // tiles, then the count and a count per chunk
+      ok = cudaMalloc(&ctx->ep_ptiles, (c + 1 + kEpMaxRanks) * sizeof(RowTile)) == cudaSuccess &&
+           cudaHostAlloc(&ctx->ep_h_ptiles, (c + 1 + kEpMaxRanks) * sizeof(RowTile),
+                         cudaHostAllocDefault) == cudaSuccess &&
            cudaMalloc(&ctx->ep_tile_out, c * sizeof(unsigned long long)) == cudaSuccess &&
            cudaHostAlloc(&ctx->ep_h_tile_out, c * sizeof(unsigned long long),
                          cudaHostAllocDefault) == cudaSuccess;
@@ -2033,45 +2058,62 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
   const __half* rows_in = static_cast<const __half*>(ctx->ep_buf[kEpRows]);
   const uint32_t* map_in = static_cast<const uint32_t*>(ctx->ep_buf[kEpMap]);
 
-  // ---- this rank's row tiles, each with its rows' destination ----
+  // ---- this rank's row tiles, each with its rows' destination, in chunks:
+  // chunk c holds the pairs of source rank (me + 1 + c) % R, the last one
+  // this rank's own pairs and its shared-expert rows.  With the copy-engine
+  // return, a remote chunk's GEMM2 rows go to this rank's expanded-row
+  // buffer (dead after GEMM1, same row order) and are copied on; else
+  // straight into the source's return buffer ----
+  const bool by_copy = ctx->ep_return == 1 && ctx->ep_chunk_ok && R > 1;
   const uint32_t rows_here = recv_pairs[me] + (sh ? T : 0u);
   RowTile* ht = ctx->ep_h_ptiles;
   unsigned long long* hto = ctx->ep_h_tile_out;
+  const size_t tcap = ctx->ep_ptiles_cap;  // tiles; counts follow at tcap, tcap + 1 + c
+  std::vector<uint32_t> chunk_first(R, 0), chunk_n(R, 0);
   uint32_t n_tiles = 0;
-  for (int q = 0; q < R && local == TSG_OK; ++q) {
+  for (int c = 0; c < R && local == TSG_OK; ++c) {
+    const int q = (me + 1 + c) % R;
+    chunk_first[c] = n_tiles;
     uint32_t row = rpo[me * R + q];    // in this rank's received pairs
     uint32_t back = soff[q * R + me];  // in q's sorted order
     __half* qret = static_cast<__half*>(ctx->ep_peer[kEpRet][q]);
     for (uint32_t j = 0; j < El; ++j) {
-      const uint32_t c = M[q * W + me * El + j];
-      for (uint32_t b = 0; b < c && local == TSG_OK; b += tr) {
-        const uint32_t rows = std::min(tr, c - b);
-        if (n_tiles + 1 >= ctx->ep_ptiles_cap ||
-            static_cast<size_t>(back + b + rows) * D > ctx->ep_caps[kEpRet][q]) {
+      const uint32_t cnt = M[q * W + me * El + j];
+      for (uint32_t b = 0; b < cnt && local == TSG_OK; b += tr) {
+        const uint32_t rows = std::min(tr, cnt - b);
+        if (n_tiles >= tcap || static_cast<size_t>(back + b + rows) * D > ctx->ep_caps[kEpRet][q]) {
           note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: tile plan exceeds a buffer"));
           break;
         }
         ht[n_tiles] = {j, row + b, rows, 0};
-        hto[n_tiles] = reinterpret_cast<unsigned long long>(qret + static_cast<size_t>(back + b) * D);
+        __half* dst = by_copy && q != me ? xp + static_cast<size_t>(row + b) * D
+                                         : qret + static_cast<size_t>(back + b) * D;
+        hto[n_tiles] = reinterpret_cast<unsigned long long>(dst);
         ++n_tiles;
       }
-      row += c;
-      back += c;
+      row += cnt;
+      back += cnt;
     }
+    if (q == me)
+      for (uint32_t b = 0; sh && b < T && local == TSG_OK; b += tr) {
+        const uint32_t rows = std::min(tr, T - b);
+        if (n_tiles >= tcap) {
+          note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: tile plan exceeds a buffer"));
+          break;
+        }
+        ht[n_tiles] = {El, recv_pairs[me] + b, rows, 0};
+        hto[n_tiles] = reinterpret_cast<unsigned long long>(ret + static_cast<size_t>(P + b) * D);
+        ++n_tiles;
+      }
+    chunk_n[c] = n_tiles - chunk_first[c];
   }
-  for (uint32_t b = 0; sh && b < T && local == TSG_OK; b += tr) {
-    const uint32_t rows = std::min(tr, T - b);
-    if (n_tiles + 1 >= ctx->ep_ptiles_cap) {
-      note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: tile plan exceeds a buffer"));
-      break;
-    }
-    ht[n_tiles] = {El, recv_pairs[me] + b, rows, 0};
-    hto[n_tiles] = reinterpret_cast<unsigned long long>(ret + static_cast<size_t>(P + b) * D);
-    ++n_tiles;
+  if (local != TSG_OK) {
+    n_tiles = 0;
+    std::fill(chunk_n.begin(), chunk_n.end(), 0u);
   }
-  if (local != TSG_OK) n_tiles = 0;
-  ht[ctx->ep_ptiles_cap].expert = n_tiles;  // the count rides after the tiles
-  ctx->ep_pntiles = &ctx->ep_ptiles[ctx->ep_ptiles_cap].expert;
+  ht[tcap].expert = n_tiles;
+  for (int c = 0; c < R; ++c) ht[tcap + 1 + c].expert = chunk_n[c];
+  ctx->ep_pntiles = &ctx->ep_ptiles[tcap].expert;
   auto cuda_note = [&](cudaError_t e, const char* where) {
     if (e != cudaSuccess) note(cuda_fail(ctx, e, where));
   };
@@ -2083,11 +2125,11 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
                               cudaMemcpyHostToDevice, s),
               "tiles");
   }
-  cuda_note(cudaMemcpyAsync(ctx->ep_pntiles, &ht[ctx->ep_ptiles_cap].expert, 4,
+  cuda_note(cudaMemcpyAsync(&ctx->ep_ptiles[tcap], &ht[tcap], (1 + R) * sizeof(RowTile),
                             cudaMemcpyHostToDevice, s),
             "tiles");
   // this rank's shared-expert rows (and the shared gate's dots) after the
-  // pairs it receives
+  // pair rows it expands
   if (sh && T > 0 && local == TSG_OK) {
     const float* gate_w = L->has_gate ? L->router_rows + static_cast<size_t>(E) * D : nullptr;
     cuda_note(launch_gather_rows_gate(static_cast<const uint16_t*>(hidden), hidden_stride,
@@ -2160,7 +2202,35 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
     qp.num_sms = ctx->num_sms;
     cuda_note(launch_qmm_gate_up(qp, s), "qmm gate/up");
     ev(5);
-    if (local == TSG_OK) cuda_note(launch_qmm_down(qp, s), "qmm down");
+    if (!by_copy) {
+      if (local == TSG_OK) cuda_note(launch_qmm_down(qp, s), "qmm down");
+    } else {
+      // a chunk per source rank; each remote chunk's rows are copied to
+      // their rank by the copy stream while the next chunk computes
+      for (int c = 0; c < R && local == TSG_OK; ++c) {
+        const int q = (me + 1 + c) % R;
+        if (chunk_n[c]) {
+          QmmParams qc = qp;
+          qc.row_tiles = ctx->ep_ptiles + chunk_first[c];
+          qc.n_row_tiles = &ctx->ep_ptiles[tcap + 1 + c].expert;
+          qc.tile_out = ctx->ep_tile_out + chunk_first[c];
+          cuda_note(launch_qmm_down(qc, s), "qmm down");
+        }
+        const uint32_t cnt = snd[q * R + me];
+        if (q != me && cnt && local == TSG_OK) {
+          cuda_note(cudaEventRecord(ctx->ep_chunk_ev[c], s), "chunk event");
+          cuda_note(cudaStreamWaitEvent(ctx->ep_copy, ctx->ep_chunk_ev[c], 0), "chunk event");
+          cuda_note(cudaMemcpyAsync(static_cast<__half*>(ctx->ep_peer[kEpRet][q]) +
+                                        static_cast<size_t>(soff[q * R + me]) * D,
+                                    xp + static_cast<size_t>(rpo[me * R + q]) * D,
+                                    static_cast<size_t>(cnt) * D * sizeof(__half),
+                                    cudaMemcpyDeviceToDevice, ctx->ep_copy),
+                    "return copy");
+        }
+      }
+      cuda_note(cudaEventRecord(ctx->ep_chunk_ev[R], ctx->ep_copy), "chunk event");
+      cuda_note(cudaStreamWaitEvent(s, ctx->ep_chunk_ev[R], 0), "chunk event");
+    }
   } else {
     ev(5);
   }
