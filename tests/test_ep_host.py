@@ -7,7 +7,10 @@ combine in rank order.  Each rank's result must equal the oracle's whole
 block for its tokens; and a failure injected on one rank's host side (in its
 routing, or in its plan and buffers) must end the call on every rank with an
 error at the next agreement point -- no rank left waiting in an exchange.
-The steps are those of tsg_ep_moe_block_forward."""
+The steps are those of tsg_ep_moe_block_forward; ep_forward_peer mirrors its
+peer-memory transport the same way (one all-gather of counts and statuses,
+a plan every rank computes alike, a growth agreed through its handle
+exchange)."""
 
 from __future__ import annotations
 
@@ -108,6 +111,105 @@ def ep_forward(layer, x_local: np.ndarray, rank: int, world: int, a2a,
     return y.astype(np.float32)
 
 
+def ep_forward_peer(layer, x_local: np.ndarray, rank: int, world: int, all_gather, a2a,
+                    caps: dict, fail_at: str | None = None) -> np.ndarray:
+    """One rank of the peer-memory transport (tsg_ep_moe_block_forward with
+    ep_transport 1).  One all-gather carries every rank's per-expert counts,
+    its token rows per owner, T and a status word; from it every rank
+    computes the same plan for all ranks (pair runs, row and map offsets in
+    each owner's buffers, every buffer's need), so a growth is decided alike
+    everywhere and its handle exchange carries a status word.  The peer
+    stores are emulated by an all-to-all whose pieces land at the offsets the
+    plan gives.  `fail_at`: "route" (before the counts go out) or "grow" (an
+    allocation of a growth)."""
+    from oracle import oracle as O
+
+    h = layer.h
+    E, K, D = h.num_experts, h.top_k, h.d
+    El = E // world
+    T = x_local.shape[0]
+    ok = True
+    counts = np.zeros(E, np.int64)
+    tok = np.zeros(world, np.int64)
+    try:
+        if fail_at == "route":
+            raise MemoryError("injected: routing launch failed")
+        ids, w, _, _ = layer.router(x_local)
+        pairs = O.make_pairs(ids)
+        g = O.group_pairs(pairs, T, K, E, 16)
+        sp = g["sorted_pairs"]
+        counts = g["counts"].astype(np.int64)
+        owner_of = ids.astype(np.int64) // El  # [T, K]
+        on = np.stack([(owner_of == o).any(axis=1) for o in range(world)])  # [world, T]
+        slots = np.where(on, np.cumsum(on, axis=1) - 1, -1)
+        tok = on.sum(axis=1)
+    except MemoryError as exc:
+        ok, local_error = False, str(exc)
+    # agreement: every rank's words
+    words = np.concatenate([counts, tok, [T, 1 if ok else 0]])
+    M = all_gather(words).reshape(world, -1)
+    if not ok:
+        raise EPError(local_error)
+    bad = [q for q in range(world) if M[q, E + world + 1] != 1]
+    if bad:
+        raise EPError(f"rank {bad[0]} failed before the row exchange")
+    # the plan, the same on every rank
+    Tq = M[:, E + world]
+    snd = np.array([[M[q, o * El:(o + 1) * El].sum() for o in range(world)] for q in range(world)])
+    soff = np.concatenate([np.zeros((world, 1), np.int64), np.cumsum(snd, axis=1)[:, :-1]], axis=1)
+    tokm = M[:, E:E + world]
+    assert (snd.sum(axis=1) == Tq * K).all()
+    rpo = np.concatenate([np.zeros((1, world), np.int64), np.cumsum(snd, axis=0)[:-1]], axis=0)  # [q, o]
+    rro = np.concatenate([np.zeros((1, world), np.int64), np.cumsum(tokm, axis=0)[:-1]], axis=0)
+    need = {"rows": tokm.sum(axis=0) * D, "map": snd.sum(axis=0), "ret": Tq * K * D}
+    grow = any((need[k] > caps[k]).any() for k in need)
+    if grow:
+        st = all_gather(np.array([0 if fail_at == "grow" else 1]))
+        bad = [q for q in range(world) if st[q] != 1]
+        if bad:
+            raise EPError(f"rank {bad[0]} could not allocate its exchange buffers")
+        for k in need:
+            caps[k] = np.maximum(caps[k], need[k] + need[k] // 4)
+    # dispatch: a token row once per owner, and each pair's row index
+    send_rows, send_map, rs, ms = [], [], [], []
+    for o in range(world):
+        toks = np.nonzero(slots[o] >= 0)[0]
+        send_rows.append(x_local[toks].astype(np.int32))
+        run = sp[soff[rank, o]:soff[rank, o] + snd[rank, o]]
+        assert (run["expert"] // El == o).all()
+        send_map.append(rro[rank, o] + slots[o][run["token"]])
+        rs.append(len(toks))
+        ms.append(len(run))
+    rr = [int(tokm[q, rank]) for q in range(world)]
+    rm = [int(snd[q, rank]) for q in range(world)]
+    rows_in = a2a(np.concatenate(send_rows).reshape(-1, D), rs, rr)
+    map_in = a2a(np.concatenate(send_map), ms, rm)
+    # the pieces land where the plan says: source q's rows at rro[q, me],
+    # its map entries at rpo[q, me]
+    assert rows_in.shape[0] == tokm[:, rank].sum() and map_in.shape[0] == snd[:, rank].sum()
+    xp = rows_in[map_in]  # the owner's expansion
+    # the owner computes its experts, one run per (source rank, local expert)
+    out = np.zeros((xp.shape[0], D), np.float32)
+    for q in range(world):
+        row = rpo[q, rank]
+        for j in range(El):
+            c = int(M[q, rank * El + j])
+            if c:
+                force = np.full((c, K), rank * El + j, np.uint32)
+                wt = np.zeros((c, K), np.float32)
+                wt[:, 0] = 1.0
+                out[row:row + c], _, _ = layer.block(xp[row:row + c].astype(np.uint16), force, wt)
+            row += c
+    # returned to each source rank at soff[q, me] of its sorted order
+    ret = a2a(out, rm, ms)
+    pos = np.empty(T * K, np.int64)
+    pos[sp["token"] * K + sp["rank"]] = np.arange(T * K)
+    y = np.zeros((T, D), np.float64)
+    for k in range(K):
+        y += w[:, k:k + 1].astype(np.float64) * ret[pos[np.arange(T) * K + k]]
+    return y.astype(np.float32)
+
+
 def _rank_main(rank: int, port: int, q, fail_rank: int = -1, fail_at: str | None = None):
     try:
         sys.path.insert(0, str(ROOT))
@@ -127,12 +229,30 @@ def _rank_main(rank: int, port: int, q, fail_rank: int = -1, fail_at: str | None
             dist.all_to_all_single(out, src, recv_splits, send_splits)
             return out.numpy().reshape((sum(recv_splits),) + tail)
 
+        def all_gather(arr):
+            src = torch.from_numpy(np.ascontiguousarray(arr, np.int64))
+            out = [torch.empty_like(src) for _ in range(WORLD)]
+            dist.all_gather(out, src)
+            return torch.cat(out).numpy()
+
         layer = O.OracleLayer(host_layer("tiny", 11))
         T = 24
         x_all = host_tokens(WORLD * T, layer.h.d, 5)
         x = np.ascontiguousarray(x_all[rank * T:(rank + 1) * T])
+        my_fail = fail_at if rank == fail_rank else None
         try:
-            got = ep_forward(layer, x, rank, WORLD, a2a, fail_at if rank == fail_rank else None)
+            if fail_at in (None, "route_peer", "grow"):
+                caps = {"rows": np.zeros(WORLD, np.int64), "map": np.zeros(WORLD, np.int64),
+                        "ret": np.zeros(WORLD, np.int64)}
+                peer_fail = "route" if my_fail == "route_peer" else my_fail
+                got = ep_forward_peer(layer, x, rank, WORLD, all_gather, a2a, caps, peer_fail)
+                if fail_at is None:  # a second call: no growth, the same result
+                    got2 = ep_forward_peer(layer, x, rank, WORLD, all_gather, a2a, caps)
+                    assert np.array_equal(got, got2)
+                    got1 = ep_forward(layer, x, rank, WORLD, a2a)
+                    assert np.allclose(got, got1, rtol=0, atol=1e-6)
+            else:
+                got = ep_forward(layer, x, rank, WORLD, a2a, my_fail)
         except EPError as exc:
             dist.destroy_process_group()
             q.put((rank, "ep_error", str(exc)))
@@ -173,7 +293,8 @@ def test_expert_parallel_protocol_on_two_gloo_ranks():
         assert payload < 1e-6, f"rank {rank}: rel L2 {payload}"
 
 
-@pytest.mark.parametrize("fail_rank,fail_at", [(1, "route"), (0, "plan")])
+@pytest.mark.parametrize("fail_rank,fail_at", [(1, "route"), (0, "plan"), (0, "route_peer"),
+                                               (1, "grow")])
 def test_a_rank_failure_ends_the_call_on_every_rank(fail_rank, fail_at):
     """A host-side failure on one rank (before its counts go out, or while it
     sizes its buffers after them) ends the call with an error on every rank
@@ -183,7 +304,9 @@ def test_a_rank_failure_ends_the_call_on_every_rank(fail_rank, fail_at):
     assert len(results) == WORLD
     for rank, status, payload in results:
         assert status == "ep_error", f"rank {rank}: {status} {payload}"
-        if rank == fail_rank:
+        if fail_at == "grow":
+            assert f"rank {fail_rank} could not allocate" in payload
+        elif rank == fail_rank:
             assert "injected" in payload
         else:
             assert f"rank {fail_rank} failed" in payload
