@@ -247,8 +247,8 @@ def run_ours(args):
             sweep.update(run_prefill_sweep(ctx, device, args))
         except Exception as exc:  # reported, never hides the headline
             sweep["prefill_error"] = repr(exc)
-    if args.pdl:
-        ctx.set_option("programmatic_launch", 1)
+    if args.no_pdl:
+        ctx.set_option("programmatic_launch", 0)
     us = distinct_experts(ctx, layers, x0, T)
     # the timed graph holds only the 30 layers; a second graph of the same
     # stack brackets each layer with CUDA events for the per-kernel time
@@ -819,7 +819,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--pdl", action="store_true", help="allow programmatic dependent launch")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="no programmatic dependent launch (the library default allows it)")
     ap.add_argument("--ncu-case", choices=["decode-t1", "small-t16", "prefill"], default=None,
                     help="run a short fixed workload for ncu instead of the benchmark")
     args = ap.parse_args()

@@ -133,8 +133,9 @@ TSG_API tsg_status tsg_ctx_set_stream(tsg_ctx ctx, void *stream);
 TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
 /* Tuning switches: "fused_decode" (1: T <= 4 runs the whole block as one
  * cooperative kernel, default; 0: router / gate-up / down kernels) and
- * "programmatic_launch" (1: allow the next kernel on the stream to launch
- * while this one finishes), "gemv_max_tokens" (router-driven batches above
+ * "programmatic_launch" (1, the default: a decode kernel lets the next
+ * one on the stream launch early and start its input-independent prologue
+ * as each SM frees up; 0: plain stream order), "gemv_max_tokens" (router-driven batches above
  * decode_max_tokens and up to this size, at most 64, run the expert products
  * as batched GEMVs; default 16, 0 for the tensor-core contraction only) and
  * "debug_phase_stamps" (a device address of

@@ -311,6 +311,55 @@ def test_fused_decode_graph_replay_is_stable(ctx, name, T):
     del g
 
 
+@pytest.mark.parametrize("name,T", [("gemma", 1), ("qwen", 1), ("gemma", 2), ("qwen", 4)])
+def test_programmatic_launch_chain_is_bit_equal(ctx, name, T):
+    """A chain of layers, each reading the previous one's output, launched
+    with programmatic dependent launch (the next grid starts before this one
+    ends and waits for it): the same bits as without, eager and from a CUDA
+    graph."""
+    lays = [layer_pair(ctx, name, 31 + l, None)[1] for l in range(6)]
+    d = lays[0].d
+    x0 = to_dev(host_tokens(T, d, 5))
+    bufs = [torch.empty((T, d), dtype=torch.bfloat16, device="cuda") for _ in lays]
+
+    def chain():
+        x = x0
+        for lay, b in zip(lays, bufs):
+            lay.forward(x, y=b)
+            x = b
+        return bufs[-1]
+
+    ctx.set_option("programmatic_launch", 0)
+    want = chain().clone()
+    ctx.sync()
+    ctx.set_option("programmatic_launch", 1)
+    try:
+        for _ in range(3):
+            got = chain()
+            ctx.sync()
+            assert torch.equal(got, want)
+        for lay in lays:
+            ctx.reserve(lay, T)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            ctx.set_stream(side)
+            with torch.cuda.graph(g, stream=side):
+                chain()
+        torch.cuda.current_stream().wait_stream(side)
+        ctx.set_stream(torch.cuda.current_stream())
+        for _ in range(5):
+            bufs[-1].zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(bufs[-1], want)
+        ctx.sync()
+        del g
+    finally:
+        ctx.set_option("programmatic_launch", 1)
+
+
 @pytest.mark.parametrize("name,T", [("tiny", 1), ("gemma", 1), ("gemma", 3), ("qwen", 1),
                                     ("qwen", 4)])
 def test_streaming_decode_matches_earlier_fused_kernel(ctx, name, T):

@@ -663,6 +663,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.stamps && tid == 0) stamp_at(p.stamps, bid * kStamps + k);
   };
   stamp(0);
+  // with programmatic launch, the next layer's grid may be launched now: its
+  // CTAs take each SM as this launch's CTA there exits, and wait
+  // (griddepcontrol.wait) for this whole grid before reading what it wrote
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ---------------- prologue: router rows (input independent) ----------------
   int my_rows = 0;
@@ -674,7 +678,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     s_issued[tid - 32] = 0;
   }
-  if (tid == 64) s_epoch = __ldcg(&sig->epoch[bid]) + 1u;  // this launch's tag
   if (tid >= 128 && tid < 128 + kMaxSlots) {
     mbar_init(&bar_ld[tid - 128], 1);
     mbar_init(&bar_slot[tid - 128], 1);
@@ -707,6 +710,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // this launch's tag, read after the previous launch has finished (with
+  // programmatic launch this CTA may start before that launch's CTA of the
+  // same index has written it)
+  if (tid == 64) s_epoch = __ldcg(&sig->epoch[bid]) + 1u;
   stamp(1);
 
   // ---------------- tokens: norm, operand fragments, accumulator starts ----------------

@@ -83,7 +83,7 @@ struct tsg_ctx_s {
   size_t f_flags_bytes = 0;
   bool use_fused = true;
   int fused_kind = 1;              // 1: streaming decode kernel, 2: the earlier fused kernel
-  bool allow_pdl = false;
+  bool allow_pdl = true;  // programmatic dependent launch of the decode kernels
   unsigned long long* stamps = nullptr;  // debug phase timestamps (device)
   // device status words: [0] error bits, [1] code, [2] value, [3] pad;
   // [4] last-CTA counter
