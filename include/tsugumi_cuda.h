@@ -138,9 +138,10 @@ TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
  * as each SM frees up; 0: plain stream order), "gemv_max_tokens" (router-driven batches above
  * decode_max_tokens and up to this size, at most 64, run the expert products
  * as batched GEMVs; default 16, 0 for the tensor-core contraction only) and
- * "debug_phase_stamps" (a device address of
- * num_sms x 8 uint64 the fused decode kernel fills with %globaltimer stamps
- * at its phase boundaries, or 0 for none), "ep_transport" (expert
+ * "debug_phase_stamps" (a device address of num_sms x 96 uint64 the
+ * streaming decode kernel fills with %globaltimer stamps at its phase
+ * boundaries, or 0 for none; only a library built with
+ * TSG_NVCC_DEFINES="-DTSG_PHASE_STAMPS=1" has the stamping code), "ep_transport" (expert
  * parallelism: 1, the default, moves rows through peer memory; 0 through
  * NCCL all-to-all; every rank of a group sets the same value) and
  * "ep_return" (peer transport: 1, the default, runs the down contraction in

@@ -44,17 +44,28 @@ def nvcc() -> str:
     return path
 
 
+def _defines() -> list[str]:
+    """Extra -D flags from TSG_NVCC_DEFINES (an instrumentation build, e.g.
+    "-DTSG_PHASE_STAMPS=1"); empty for the product."""
+    return [d for d in os.environ.get("TSG_NVCC_DEFINES", "").split() if d.startswith("-D")]
+
+
 def _compile(src: Path, verbose_ptxas: bool) -> Path:
     obj = BUILD / (src.stem + ".o")
     deps = [src] + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "tsugumi_cuda.h"]
-    if obj.exists() and all(obj.stat().st_mtime >= d.stat().st_mtime for d in deps):
+    stamp = BUILD / (src.stem + ".defines")
+    defines = _defines()
+    same_defines = stamp.exists() and stamp.read_text() == " ".join(defines)
+    if (obj.exists() and same_defines and
+            all(obj.stat().st_mtime >= d.stat().st_mtime for d in deps)):
         return obj
-    cmd = [nvcc(), *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+    cmd = [nvcc(), *NVCC_FLAGS, *defines, "-c", str(src), "-o", str(obj)]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{res.stderr}")
+    stamp.write_text(" ".join(defines))
     if verbose_ptxas:
         sys.stderr.write(res.stderr)
     return obj

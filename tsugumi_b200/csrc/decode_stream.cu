@@ -308,7 +308,18 @@ TSG_DEV int qdiv(int a, float inv_b) {
   return __float2int_rz((static_cast<float>(a) + 0.5f) * inv_b);
 }
 
-TSG_DEV void stamp_at(unsigned long long* stamps, int idx) { stamps[idx] = global_timer_ns(); }
+// Phase time stamps (the "debug_phase_stamps" option) exist only in a build
+// with TSG_PHASE_STAMPS=1 (TSG_NVCC_DEFINES="-DTSG_PHASE_STAMPS=1" for the
+// package build); otherwise their code is not in the kernel, which is
+// measurably faster without it (the kernel's one-pass code runs from a cold
+// instruction cache).
+#ifndef TSG_PHASE_STAMPS
+#define TSG_PHASE_STAMPS 0
+#endif
+constexpr bool kPhaseStamps = TSG_PHASE_STAMPS != 0;
+TSG_DEV void stamp_at(unsigned long long* stamps, int idx) {
+  if (kPhaseStamps) stamps[idx] = global_timer_ns();
+}
 
 // Bounded wait on an mbarrier phase that ignores the error word: used only
 // to let this CTA's own copies land before it exits after an error.
@@ -660,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* red = reinterpret_cast<float*>(smem + L.red_off);
   uint8_t* ring = smem + L.ring_off;
   auto stamp = [&](int k) {
-    if (p.stamps && tid == 0) stamp_at(p.stamps, bid * kStamps + k);
+    if (kPhaseStamps && p.stamps && tid == 0) stamp_at(p.stamps, bid * kStamps + k);
   };
   stamp(0);
   // with programmatic launch, the next layer's grid may be launched now: its
@@ -1486,7 +1497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         par ^= 1u;
-        if (lane == 0 && p.stamps && j < 8) stamp_at(p.stamps, bid * kStamps + 48 + j);  // debug
+        if (kPhaseStamps && lane == 0 && p.stamps && j < 8) stamp_at(p.stamps, bid * kStamps + 48 + j);  // debug
         const unsigned long long* wv = wstg + static_cast<size_t>(j) * (F / 2);
         bool ok = true;
         for (int w = lane; w < F / 2; w += 32) ok &= static_cast<uint32_t>(wv[w] >> 32) == tag;
@@ -1517,7 +1528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&bar_slot[j]);
-        if (p.stamps && j < 8) stamp_at(p.stamps, bid * kStamps + 32 + j);  // debug: slot in
+        if (kPhaseStamps && p.stamps && j < 8) stamp_at(p.stamps, bid * kStamps + 32 + j);  // debug: slot in
       }
     }
     // 2. this warp's down units, slot by slot, as the slots come in
@@ -1612,7 +1623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             st_relaxed_u64(o + 3, tg | fr.w);
           }
           __syncwarp();
-          if (s < 8 && lane == 0 && p.stamps) stamp_at(p.stamps, bid * kStamps + 48 + s);  // debug
+          if (kPhaseStamps && s < 8 && lane == 0 && p.stamps) stamp_at(p.stamps, bid * kStamps + 48 + s);  // debug
 
         } else if (lane < T) {
           // four (tag, half2) words: a reader that sees this launch's tag in
@@ -1635,7 +1646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           st_relaxed_u32(p.gdone + bid, tag);
           __threadfence();
-          if (p.stamps) stamp_at(p.stamps, bid * kStamps + 11);  // debug: acts out
+          if (kPhaseStamps && p.stamps) stamp_at(p.stamps, bid * kStamps + 11);  // debug: acts out
         }
         __syncwarp();
       }
@@ -1648,7 +1659,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every stage is released, so the ring is free: each slot's tagged act
       // words in one bulk copy, all requested at once (the compute warps
       // check, unpack and release them)
-      if (p.stamps) stamp_at(p.stamps, bid * kStamps + 40);  // debug: loads start
+      if (kPhaseStamps && p.stamps) stamp_at(p.stamps, bid * kStamps + 40);  // debug: loads start
       const uint32_t sbytes = static_cast<uint32_t>(F) * 4u;  // F / 2 words
       for (int j = 0; j < nslots; ++j) {
         mbar_arrive_expect_tx(&bar_ld[j], sbytes);
