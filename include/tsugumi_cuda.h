@@ -135,7 +135,13 @@ TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
  * cooperative kernel, default; 0: router / gate-up / down kernels) and
  * "programmatic_launch" (1, the default: a decode kernel lets the next
  * one on the stream launch early and start its input-independent prologue
- * as each SM frees up; 0: plain stream order), "gemv_max_tokens" (router-driven batches above
+ * as each SM frees up; 0: plain stream order), "cooperative_launch" (1, the
+ * default: decode kernels are launched cooperatively, so the driver checks
+ * that all their CTAs are resident at once; 0 launches them plainly -- one
+ * CTA per SM on an otherwise idle GPU, every cross-CTA wait bounded -- which
+ * lets a programmatic launch start the next layer's CTAs as this one's exit,
+ * ~3 µs per layer less between eagerly launched layers; no change inside a
+ * CUDA graph), "gemv_max_tokens" (router-driven batches above
  * decode_max_tokens and up to this size, at most 64, run the expert products
  * as batched GEMVs; default 16, 0 for the tensor-core contraction only) and
  * "debug_phase_stamps" (a device address of num_sms x 96 uint64 the

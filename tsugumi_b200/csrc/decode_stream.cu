@@ -2048,7 +2048,7 @@ cudaError_t launch_decode_stream(const DecodeFusedArgs& a, const DecodeMaps& map
   cfg.stream = s;
   cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeCooperative;
-  attrs[0].val.cooperative = 1;
+  attrs[0].val.cooperative = a.cooperative ? 1 : 0;
   attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[1].val.programmaticStreamSerializationAllowed = a.allow_pdl ? 1 : 0;
   cfg.attrs = attrs;

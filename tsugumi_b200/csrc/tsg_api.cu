@@ -84,6 +84,7 @@ struct tsg_ctx_s {
   bool use_fused = true;
   int fused_kind = 1;              // 1: streaming decode kernel, 2: the earlier fused kernel
   bool allow_pdl = true;  // programmatic dependent launch of the decode kernels
+  bool cooperative = true;  // decode kernels launched with the cooperative attribute
   unsigned long long* stamps = nullptr;  // debug phase timestamps (device)
   // device status words: [0] error bits, [1] code, [2] value, [3] pad;
   // [4] last-CTA counter
@@ -468,6 +469,7 @@ tsg_status run_decode_fused(tsg_ctx ctx, tsg_moe_layer_s* L, const void* x, uint
   a.err = ctx->rb.err;
   a.num_sms = ctx->num_sms;
   a.allow_pdl = ctx->allow_pdl ? 1 : 0;
+  a.cooperative = ctx->cooperative ? 1 : 0;
   a.stamps = ctx->stamps;
   if (stream_ok(ctx, L, T)) {
     TSG_CUDA_TRY(ctx, launch_decode_stream(a, L->dmaps, ctx->f_stream, ctx->f_flags, ctx->stream),
@@ -928,6 +930,7 @@ tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char* name, int64_t value) {
     ctx->fused_kind = value == 2 ? 2 : 1;
   }
   else if (n == "programmatic_launch") ctx->allow_pdl = value != 0;
+  else if (n == "cooperative_launch") ctx->cooperative = value != 0;
   else if (n == "gemv_max_tokens") ctx->gemv_max_tokens = static_cast<uint32_t>(value < 0 ? 0 : value);
   else if (n == "ep_return") {
     // every rank of a group sets the same value (it changes no collective)

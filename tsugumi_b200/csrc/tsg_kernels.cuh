@@ -207,6 +207,7 @@ struct DecodeFusedArgs {
   uint32_t* err;
   int num_sms;
   int allow_pdl;
+  int cooperative;  // launch with the cooperative attribute (co-residency checked by the driver)
   unsigned long long* stamps;  // debug phase timestamps [grid][8], or nullptr
 };
 // decode_stream.cu: the same block, streaming every selected weight byte in
