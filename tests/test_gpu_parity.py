@@ -311,12 +311,13 @@ def test_fused_decode_graph_replay_is_stable(ctx, name, T):
     del g
 
 
-@pytest.mark.parametrize("name,T", [("gemma", 1), ("qwen", 1), ("gemma", 2), ("qwen", 4)])
-def test_programmatic_launch_chain_is_bit_equal(ctx, name, T):
+@pytest.mark.parametrize("name,T,coop", [("gemma", 1, 1), ("qwen", 1, 1), ("gemma", 2, 1),
+                                         ("qwen", 4, 1), ("gemma", 1, 0), ("qwen", 3, 0)])
+def test_programmatic_launch_chain_is_bit_equal(ctx, name, T, coop):
     """A chain of layers, each reading the previous one's output, launched
     with programmatic dependent launch (the next grid starts before this one
-    ends and waits for it): the same bits as without, eager and from a CUDA
-    graph."""
+    ends and waits for it), cooperatively or not: the same bits as a plain
+    cooperative launch, eager and from a CUDA graph."""
     lays = [layer_pair(ctx, name, 31 + l, None)[1] for l in range(6)]
     d = lays[0].d
     x0 = to_dev(host_tokens(T, d, 5))
@@ -333,6 +334,7 @@ def test_programmatic_launch_chain_is_bit_equal(ctx, name, T):
     want = chain().clone()
     ctx.sync()
     ctx.set_option("programmatic_launch", 1)
+    ctx.set_option("cooperative_launch", coop)
     try:
         for _ in range(3):
             got = chain()
@@ -358,6 +360,7 @@ def test_programmatic_launch_chain_is_bit_equal(ctx, name, T):
         del g
     finally:
         ctx.set_option("programmatic_launch", 1)
+        ctx.set_option("cooperative_launch", 1)
 
 
 @pytest.mark.parametrize("name,T", [("tiny", 1), ("gemma", 1), ("gemma", 3), ("qwen", 1),
