@@ -153,7 +153,10 @@ TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
  * "ep_return" (peer transport: 1, the default, runs the down contraction in
  * one chunk per source rank and copies each finished chunk to its rank with
  * the copy engines while the next computes; 0 lets the contraction's
- * epilogue store the rows into the peers' buffers). */
+ * epilogue store the rows into the peers' buffers) and "ep_dispatch" (peer
+ * transport, every rank alike: 0, the default, lets the dispatch kernel
+ * store the token rows into the owners' buffers; 1 converts the rows for
+ * each remote owner into one local run and sends it with the copy engines). */
 TSG_API tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char *name, int64_t value);
 /* Pre-allocates the workspace for up to max_tokens tokens of this layer's
  * shape, so later calls allocate nothing (required before stream capture). */

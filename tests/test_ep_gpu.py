@@ -24,9 +24,11 @@ CASES = [
     ("qwen", 300, None),
     ("gemma_dense", 200, 1.1),
 ]
-# (transport, return): peer memory with the outputs returned by the copy
-# engines, peer memory with GEMM2's epilogue storing them, NCCL all-to-all
-TRANSPORTS = ((1, 1), (1, 0), (0, 1))
+# (transport, return, dispatch): peer memory as by default (rows stored by
+# the dispatch kernel, outputs returned by the copy engines); peer memory
+# with both moved by the copy engines; with both stored by kernels (GEMM2's
+# epilogue for the outputs); NCCL all-to-all
+TRANSPORTS = ((1, 1, 0), (1, 1, 1), (1, 0, 0), (0, 1, 0))
 
 
 def _free_port() -> int:
@@ -55,9 +57,10 @@ def _rank_main(rank: int, port: int, q):
         ctx.set_option("gemv_max_tokens", 0)
         group = ep.ExpertParallelGroup.from_torch_distributed(ctx)
         msgs = []
-        for transport, ret in TRANSPORTS:
+        for transport, ret, disp in TRANSPORTS:
             ctx.set_option("ep_transport", transport)
             ctx.set_option("ep_return", ret)
+            ctx.set_option("ep_dispatch", disp)
             for name, T0, skew in CASES:
                 t = device_layer_tensors(name, 4242, skew, dev)
                 full = tb.MoELayer(ctx, t)
@@ -73,7 +76,8 @@ def _rank_main(rank: int, port: int, q):
                 ctx.sync()
                 same = torch.equal(got, want) and torch.equal(got2, want)
                 diff = float((got - want).abs().max())
-                msgs.append((f"{name} transport {transport} return {ret}", same, diff))
+                msgs.append((f"{name} transport {transport} return {ret} dispatch {disp}", same,
+                             diff))
                 if transport == 1:
                     ph = shard.phase_ms()
                     msgs.append((f"{name} phases", all(v >= 0 for v in ph.values()), 0.0))

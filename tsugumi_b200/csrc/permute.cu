@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
       flag_error(d.err, TSG_DEVERR_BOUNDS);
       continue;
     }
-    d.map[o][e] = d.row0[o] + slot;
+    d.map[o][e] = d.map_base[o] + slot;
   }
   const uint32_t w = gtid >> 5;
   const int lane = threadIdx.x & 31;

@@ -120,10 +120,11 @@ struct tsg_ctx_s {
   // rank's capacities, the same on every rank (each is a function of the
   // exchanged counts); ep_peer the views of the peers' buffers.
   int ep_transport = 1;                // 0: NCCL all-to-all; 1: peer memory
-  void* ep_buf[5] = {};
-  size_t ep_buf_elems[5] = {};         // this rank's allocations
-  std::vector<size_t> ep_caps[6];      // [kind][world] elements; [5]: row tiles
-  std::vector<void*> ep_peer[5];       // [kind][world]; own entry = own buffer
+  int ep_dispatch = 0;                 // 0: rows stored by the dispatch kernel; 1: staged and copied
+  void* ep_buf[6] = {};
+  size_t ep_buf_elems[6] = {};         // this rank's allocations
+  std::vector<size_t> ep_caps[7];      // [kind][world] elements; [6]: row tiles
+  std::vector<void*> ep_peer[6];       // [kind][world]; own entry = own buffer
   uint32_t* ep_slots = nullptr;        // [world][T] token slots per owner
   size_t ep_slots_cap = 0;
   uint32_t* ep_ag = nullptr;           // device: send [kAgWords], receive [world][kAgWords], barriers
@@ -696,9 +697,12 @@ tsg_status nccl_fail(tsg_ctx ctx, ncclResult_t r, const char* where) {
     if (r__ != ncclSuccess) return nccl_fail(ctx, r__, where);      \
   } while (0)
 
-enum EpBuf { kEpXp = 0, kEpAct, kEpRet, kEpRows, kEpMap, kEpBufs };
-constexpr size_t kEpElemBytes[kEpBufs] = {2, 2, 2, 2, 4};
-constexpr bool kEpShared[kEpBufs] = {false, false, true, true, true};  // written by peers
+// kEpStage: this rank's token rows for its remote owners, one contiguous
+// run per owner, before the copy engines send them
+enum EpBuf { kEpXp = 0, kEpAct, kEpRet, kEpRows, kEpMap, kEpStage, kEpBufs };
+constexpr int kEpTiles = kEpBufs, kEpKinds = kEpBufs + 1;  // capacities: buffers, then row tiles
+constexpr size_t kEpElemBytes[kEpBufs] = {2, 2, 2, 2, 4, 2};
+constexpr bool kEpShared[kEpBufs] = {false, false, true, true, true, false};  // written by peers
 
 // Unmaps the peers' buffers (the peers keep their own) and forgets every
 // rank's capacities, so the next call grows them all again.
@@ -936,6 +940,11 @@ tsg_status tsg_ctx_set_option(tsg_ctx ctx, const char* name, int64_t value) {
     // every rank of a group sets the same value (it changes no collective)
     if (value != 0 && value != 1) return fail(ctx, TSG_ERR_INVALID_ARG, "ep_return is 0 or 1");
     ctx->ep_return = static_cast<int>(value);
+  }
+  else if (n == "ep_dispatch") {
+    // every rank of a group sets the same value (it enters the plan)
+    if (value != 0 && value != 1) return fail(ctx, TSG_ERR_INVALID_ARG, "ep_dispatch is 0 or 1");
+    ctx->ep_dispatch = static_cast<int>(value);
   }
   else if (n == "ep_transport") {
     // every rank of a group must pass the same value before its next call
@@ -1912,7 +1921,7 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
   const uint32_t tr = static_cast<uint32_t>(qmm_tile_rows());
   std::vector<uint32_t> Tq(R), snd(R * R), soff(R * R), rpo(R * R), tok(R * R), rro(R * R);
   std::vector<uint32_t> recv_pairs(R), recv_rows(R);
-  std::vector<size_t> need[6];
+  std::vector<size_t> need[kEpKinds];
   for (std::vector<size_t>& v : need) v.assign(R, 0);
   bool sums_ok = true;
   for (int q = 0; q < R; ++q) {
@@ -1949,7 +1958,11 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
     need[kEpRet][o] = (static_cast<size_t>(Tq[o]) * K + (sh ? Tq[o] : 0u)) * D;
     need[kEpRows][o] = rows * D;
     need[kEpMap][o] = acc;
-    need[5][o] = tiles + (sh ? (Tq[o] + tr - 1) / tr : 0u);
+    need[kEpTiles][o] = tiles + (sh ? (Tq[o] + tr - 1) / tr : 0u);
+    uint64_t staged = 0;  // rows rank o stages for its remote owners
+    for (int q = 0; q < R; ++q)
+      if (q != o) staged += tok[o * R + q];
+    need[kEpStage][o] = ctx->ep_dispatch == 1 ? staged * D : 0u;
   }
   if (!sums_ok) return fail(ctx, TSG_ERR_UNSUPPORTED_SHAPE, "expert-parallel: too many pairs");
 
@@ -1957,16 +1970,16 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
   // is short, publish the handles of the buffers peers write, map the
   // peers', agree ----
   bool grow_all = false;
-  for (int b = 0; b < 6; ++b)
+  for (int b = 0; b < kEpKinds; ++b)
     for (int r = 0; r < R; ++r)
       if (need[b][r] > ctx->ep_caps[b][r]) grow_all = true;
   if (grow_all) {
-    std::vector<size_t> cap[6];
-    for (int b = 0; b < 6; ++b) {
+    std::vector<size_t> cap[kEpKinds];
+    for (int b = 0; b < kEpKinds; ++b) {
       cap[b].resize(R);
       for (int r = 0; r < R; ++r) {
         const size_t nd = need[b][r], c = ctx->ep_caps[b][r];
-        cap[b][r] = nd > c ? std::max<size_t>(nd + nd / 4, b == 5 ? 256u : 1u << 16) : c;
+        cap[b][r] = nd > c ? std::max<size_t>(nd + nd / 4, b == kEpTiles ? 256u : 1u << 16) : c;
       }
     }
     close_peer_views(ctx);
@@ -1979,14 +1992,14 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
     // no rank maps another's buffers now
     bool ok = true;
     for (int b = 0; b < kEpBufs && ok; ++b) {
-      if (cap[b][me] <= ctx->ep_buf_elems[b] && ctx->ep_buf[b]) continue;
+      if (cap[b][me] <= ctx->ep_buf_elems[b] && (ctx->ep_buf[b] || cap[b][me] == 0)) continue;
       if (ctx->ep_buf[b]) cudaFree(ctx->ep_buf[b]);
       ctx->ep_buf[b] = nullptr;
       ctx->ep_buf_elems[b] = 0;
       ok = cudaMalloc(&ctx->ep_buf[b], cap[b][me] * kEpElemBytes[b]) == cudaSuccess;
       if (ok) ctx->ep_buf_elems[b] = cap[b][me];
     }
-    if (ok && (!ctx->ep_ptiles || ctx->ep_ptiles_cap < cap[5][me] + 1)) {
+    if (ok && (!ctx->ep_ptiles || ctx->ep_ptiles_cap < cap[kEpTiles][me] + 1)) {
       for (void* p : {static_cast<void*>(ctx->ep_ptiles), static_cast<void*>(ctx->ep_tile_out)})
         if (p) cudaFree(p);
       for (void* p : {static_cast<void*>(ctx->ep_h_ptiles), static_cast<void*>(ctx->ep_h_tile_out)})
@@ -1994,7 +2007,7 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
       ctx->ep_ptiles = ctx->ep_h_ptiles = nullptr;
       ctx->ep_tile_out = ctx->ep_h_tile_out = nullptr;
       ctx->ep_ptiles_cap = 0;
-      const size_t c = cap[5][me] + 1;  // tiles, then the count and a count per chunk
+      const size_t c = cap[kEpTiles][me] + 1;  // tiles, then the count and a count per chunk
       ok = cudaMalloc(&ctx->ep_ptiles, (c + 1 + kEpMaxRanks) * sizeof(RowTile)) == cudaSuccess &&
            cudaHostAlloc(&ctx->ep_h_ptiles, (c + 1 + kEpMaxRanks) * sizeof(RowTile),
                          cudaHostAllocDefault) == cudaSuccess &&
@@ -2053,7 +2066,7 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
       return fail(ctx, TSG_ERR_CUDA, "expert-parallel: rank " + std::to_string(first_bad) +
                                          " could not map its peers' buffers");
     }
-    for (int b = 0; b < 6; ++b) ctx->ep_caps[b] = cap[b];
+    for (int b = 0; b < kEpKinds; ++b) ctx->ep_caps[b] = cap[b];
   }
   __half* xp = static_cast<__half*>(ctx->ep_buf[kEpXp]);
   __half* act = static_cast<__half*>(ctx->ep_buf[kEpAct]);
@@ -2145,6 +2158,7 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
   ev(2);
   // ---- dispatch: each token row once to every owner of one of its
   // experts, and each pair's row index, into the owners' buffers ----
+  const bool staged_dispatch = ctx->ep_dispatch == 1 && ctx->ep_chunk_ok && R > 1;
   if (P > 0 && local == TSG_OK) {
     EpDispatch d{};
     d.x = static_cast<const uint16_t*>(hidden);
@@ -2157,11 +2171,27 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
     d.D = static_cast<int>(D);
     d.experts_per_rank = static_cast<int>(El);
     d.world = R;
+    // with staging, the rows for a remote owner o go to this rank's stage
+    // buffer (run st_off[o]) and the copy engines move each run; the map
+    // entries (4 bytes a pair) are stored into the owners' maps directly
+    std::vector<uint32_t> st_off(R, 0);
+    uint32_t st_rows = 0;
+    for (int o = 0; o < R; ++o)
+      if (staged_dispatch && o != me) {
+        st_off[o] = st_rows;
+        st_rows += tok[me * R + o];
+      }
+    __half* stage = static_cast<__half*>(ctx->ep_buf[kEpStage]);
     for (int o = 0; o < R; ++o) {
-      d.rows[o] = static_cast<__half*>(ctx->ep_peer[kEpRows][o]);
+      const bool st = staged_dispatch && o != me;
+      d.rows[o] = st ? stage + static_cast<size_t>(st_off[o]) * D
+                     : static_cast<__half*>(ctx->ep_peer[kEpRows][o]);
       d.map[o] = static_cast<uint32_t*>(ctx->ep_peer[kEpMap][o]);
-      d.row0[o] = rro[o * R + me];
-      d.row_cap[o] = static_cast<uint32_t>(std::min<size_t>(ctx->ep_caps[kEpRows][o] / D, UINT32_MAX));
+      d.row0[o] = st ? 0u : rro[o * R + me];
+      d.row_cap[o] = st ? tok[me * R + o]
+                        : static_cast<uint32_t>(std::min<size_t>(ctx->ep_caps[kEpRows][o] / D,
+                                                                 UINT32_MAX));
+      d.map_base[o] = rro[o * R + me];
       d.n_rows[o] = tok[me * R + o];
       d.map0[o] = rpo[o * R + me];
       d.map_cap[o] = static_cast<uint32_t>(std::min<size_t>(ctx->ep_caps[kEpMap][o], UINT32_MAX));
@@ -2169,7 +2199,26 @@ tsg_status ep_peer_forward(tsg_ctx ctx, tsg_moe_layer L, const void* hidden,
       d.send_cnt[o] = snd[me * R + o];
     }
     d.err = rb.err;
-    cuda_note(launch_ep_dispatch(d, s), "dispatch");
+    if (staged_dispatch && static_cast<size_t>(st_rows) * D > ctx->ep_buf_elems[kEpStage])
+      note(fail(ctx, TSG_ERR_CUDA, "expert-parallel: stage buffer too small"));
+    if (local == TSG_OK) cuda_note(launch_ep_dispatch(d, s), "dispatch");
+    if (staged_dispatch && local == TSG_OK) {
+      cuda_note(cudaEventRecord(ctx->ep_chunk_ev[0], s), "stage event");
+      cuda_note(cudaStreamWaitEvent(ctx->ep_copy, ctx->ep_chunk_ev[0], 0), "stage event");
+      for (int c = 1; c < R; ++c) {  // (rotated: at any moment the ranks send to different owners)
+        const int o = (me + c) % R;
+        const uint32_t cnt = tok[me * R + o];
+        if (cnt)
+          cuda_note(cudaMemcpyAsync(static_cast<__half*>(ctx->ep_peer[kEpRows][o]) +
+                                        static_cast<size_t>(rro[o * R + me]) * D,
+                                    stage + static_cast<size_t>(st_off[o]) * D,
+                                    static_cast<size_t>(cnt) * D * sizeof(__half),
+                                    cudaMemcpyDeviceToDevice, ctx->ep_copy),
+                    "dispatch copy");
+      }
+      cuda_note(cudaEventRecord(ctx->ep_chunk_ev[R], ctx->ep_copy), "stage event");
+      cuda_note(cudaStreamWaitEvent(s, ctx->ep_chunk_ev[R], 0), "stage event");
+    }
   }
   {
     bool all_ok = false;

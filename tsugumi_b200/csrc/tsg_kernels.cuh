@@ -137,9 +137,10 @@ constexpr uint32_t kEpNoSlot = 0xFFFFFFFFu;
 cudaError_t launch_ep_owner_slots(const uint32_t* ids, int T, int K, int experts_per_rank,
                                   int world, uint32_t* slots, uint32_t* counts, cudaStream_t s);
 // The dispatch writes the token's fp16 row (gather_rows_kernel's conversion)
-// to row row0[o] + slot of rows[o], and for pair i of this rank's sorted
-// order, owned by o, the row's index to entry map0[o] + (i - send_off[o]) of
-// map[o] -- the owner's buffers, in peer or local memory.
+// to row row0[o] + slot of rows[o] (the owner's buffer, or a local run that
+// is copied there), and for pair i of this rank's sorted order, owned by o,
+// the row's index in the owner's buffer, map_base[o] + slot, to entry
+// map0[o] + (i - send_off[o]) of map[o].
 struct EpDispatch {
   const uint16_t* x;
   uint32_t x_stride;
@@ -150,6 +151,7 @@ struct EpDispatch {
   __half* rows[kEpMaxRanks];
   uint32_t* map[kEpMaxRanks];
   uint32_t row0[kEpMaxRanks], row_cap[kEpMaxRanks], n_rows[kEpMaxRanks];  // rows: first, capacity, sent
+  uint32_t map_base[kEpMaxRanks];  // a pair's map entry: map_base[o] + the token's slot
   uint32_t map0[kEpMaxRanks], map_cap[kEpMaxRanks];
   uint32_t send_off[kEpMaxRanks], send_cnt[kEpMaxRanks];  // this rank's pairs to o
   uint32_t* err;
