@@ -1126,9 +1126,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Once its gate/up stages are done, the reduction warp bulk-loads every
   // slot's tagged act words into the (then free) ring, checks the tags
   // (loading again a slot with a word not out yet), unpacks the acts and
-  // their accumulator starts next to them and releases the slot; a compute
-  // warp has at most one down unit per slot (unit u of slot j goes to warp
-  // (j U + u) mod 15) and runs it from shared memory once the slot is in.
+  // their accumulator starts next to them and releases the slot; every warp
+  // (the reduction warp too, once its copies are requested) has at most one
+  // down unit per slot (unit u of slot j goes to warp (j U + u) mod 16) and
+  // runs it from shared memory once the slot is in.
   const int wr0 = 4 * ((bid * (D / 4)) / G);
   const int wnr = 4 * (((bid + 1) * (D / 4)) / G) - wr0;
   const int wU = ((wnr + 15) / 16) * kParts;
@@ -1542,7 +1543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     stamp(42);  // debug: warp 0 sees the down rows
     int dbg_k = 0;
     for (int j = 0; j < nslots && !failed; ++j) {
-      const int u = ((warp - j * wU) % kWarps + kWarps) % kWarps;
+      const int u = ((warp - j * wU) % kAllWarps + kAllWarps) % kAllWarps;
       if (u >= wU) continue;
       if (!__all_sync(0xFFFFFFFFu, mbar_sleep(&bar_slot[j], 0, err))) {
         failed = true;
@@ -1668,6 +1669,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&bar_ld[j], sbytes);
         bulk_load(wstg + static_cast<size_t>(j) * (F / 2), p.hact + static_cast<size_t>(j) * (F / 2),
                   sbytes, &bar_ld[j]);
+      }
+    }
+    // then this warp runs down units too (the round goes over all 16
+    // warps: a CTA of 20 rows and eight slots gives every warp one unit)
+    if (waves && !failed) {
+      if (!__all_sync(0xFFFFFFFFu, mbar_sleep(&bar_down, 0, err))) failed = true;
+      for (int j = 0; j < nslots && !failed; ++j) {
+        const int u = ((warp - j * wU) % kAllWarps + kAllWarps) % kAllWarps;
+        if (u >= wU) continue;
+        if (!__all_sync(0xFFFFFFFFu, mbar_sleep(&bar_slot[j], 0, err))) {
+          failed = true;
+          break;
+        }
+        wave_unit(wrow, j, u / kParts, u % kParts, wact, wast, lane);
       }
     }
   }
