@@ -392,7 +392,7 @@ def run_ours(args):
 
 def run_decode_sweep(ctx, layers, device, args, barrier):
     """Decode at T = 4, 8, 16, 32, 64 on the same 30-layer stack (CUDA
-    graphs): the fused kernel up to T=4, the batched GEMVs up to the context's
+    graphs): the fused kernel up to T=3, the batched GEMVs up to the context's
     gemv_max_tokens (16), the tensor-core contraction above."""
     import torch
 
@@ -409,7 +409,7 @@ def run_decode_sweep(ctx, layers, device, args, barrier):
         del g
         bytes_ = float(np.mean(us)) * EXPERT_BYTES * LAYERS
         gbs = bytes_ / (ms / 1e3) / 1e9
-        path = "fused" if T <= 4 else ("gemv" if T <= 16 else "contraction")
+        path = "fused" if T <= 3 else ("gemv" if T <= 16 else "contraction")
         out[f"decode_T{T}"] = {"layer_tokens_per_s": T * LAYERS / (ms / 1e3), "ms_per_step": ms,
                                "u_mean": float(np.mean(us)), "expert_gbs": gbs,
                                "hbm_frac": gbs / pk["hbm_gbs"], "path": path}

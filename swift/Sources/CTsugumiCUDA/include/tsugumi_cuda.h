@@ -128,8 +128,9 @@ TSG_API int tsg_abi_version(void);
 TSG_API tsg_status tsg_ctx_create(int device, void *stream, tsg_ctx *out);
 TSG_API tsg_status tsg_ctx_destroy(tsg_ctx ctx);
 TSG_API tsg_status tsg_ctx_set_stream(tsg_ctx ctx, void *stream);
-/* Largest T handled by the decode regime; default 4 (the single fused
- * kernel).  Larger T goes to the grouped tcgen05 contraction. */
+/* Largest T handled by the decode regime; default 3 (the single streaming
+ * kernel; at most 4).  Larger T goes to the batched GEMVs (up to
+ * "gemv_max_tokens") or the grouped tcgen05 contraction. */
 TSG_API tsg_status tsg_ctx_set_decode_max_tokens(tsg_ctx ctx, uint32_t t);
 /* Tuning switches: "fused_decode" (1: T <= 4 runs the whole block as one
  * cooperative kernel, default; 0: router / gate-up / down kernels) and

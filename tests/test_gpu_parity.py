@@ -64,7 +64,7 @@ class regime:
         self.ctx.set_option("gemv_max_tokens", self.gemv)
 
     def __exit__(self, *exc):
-        self.ctx.set_decode_max_tokens(4)
+        self.ctx.set_decode_max_tokens(3)  # the library's default
         self.ctx.set_option("fused_decode", 1)
         self.ctx.set_option("gemv_max_tokens", 16)
 
@@ -330,6 +330,7 @@ def test_programmatic_launch_chain_is_bit_equal(ctx, name, T, coop):
             x = b
         return bufs[-1]
 
+    ctx.set_decode_max_tokens(4)  # the decode kernels for every T here
     ctx.set_option("programmatic_launch", 0)
     want = chain().clone()
     ctx.sync()
@@ -361,6 +362,7 @@ def test_programmatic_launch_chain_is_bit_equal(ctx, name, T, coop):
     finally:
         ctx.set_option("programmatic_launch", 1)
         ctx.set_option("cooperative_launch", 1)
+        ctx.set_decode_max_tokens(3)
 
 
 @pytest.mark.parametrize("name,T", [("tiny", 1), ("gemma", 1), ("gemma", 3), ("qwen", 1),
@@ -373,12 +375,10 @@ def test_streaming_decode_matches_earlier_fused_kernel(ctx, name, T):
     xd = to_dev(host_tokens(T, host.d, 500 + T))
     ys = []
     for kind in (1, 2):
-        ctx.set_option("fused_decode", kind)
-        try:
+        with regime(ctx, dmax=4, gemv=16):
+            ctx.set_option("fused_decode", kind)
             ys.append(dev.forward(xd, out_dtype=torch.float32))
             ctx.sync()
-        finally:
-            ctx.set_option("fused_decode", 1)
     err = rel_l2(ys[0].cpu().numpy(), ys[1].cpu().numpy())
     print(f"{name} T={T}: streaming vs earlier fused rel L2 {err:.3e}")
     assert err < REL_L2
