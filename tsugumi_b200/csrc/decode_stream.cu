@@ -582,7 +582,7 @@ struct WaveRows {
   int F, K, nr;         // nr rows (in at most two 16-row tiles)
 };
 
-// One down unit of slot j -- 16-row tile t, quarter kp of K -- from the
+// One down unit of slot j -- 16-row tile t, K part kp (of kParts) -- from the
 // slot's acts in shared memory (act: [slots][F / 8] operand chunks, ast:
 // [slots][F / 32] accumulator starts), the arithmetic of the rows-owned
 // regime for one token.
@@ -1703,7 +1703,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (waves) {
     // ---------------- this CTA's rows of y (one token) ----------------
-    // v = the K quarters of a row added in order; y = residual + gate *
+    // v = the K parts of a row added in order; y = residual + gate *
     // shared + sum over ranks (ascending) w * v.  As with owned rows, the
     // next launch's grid counter is cleared all the same.
     if (bid == 0 && tid == 0) sig->gcount[(tag & 1u) ^ 1u] = 0u;
